@@ -1,0 +1,549 @@
+// C ABI entry points (include/rfsn_b200.h): argument checking, kernel
+// selection, split-KV sizing, TMA descriptor management and the small
+// utility kernels (row copies are in ring.cu, attention in *_attn.cu).
+#include <atomic>
+#include <chrono>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <thread>
+
+#include "attn_common.cuh"
+#include "params.cuh"
+
+namespace rfsn {
+
+static thread_local std::string g_last_error;
+
+void set_error(const char* fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+}
+
+static std::atomic<uint64_t> g_launches{0};
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+rfsn_status cuda_status(cudaError_t e, const char* what) {
+    set_error("%s failed: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+    return RFSN_ERR_CUDA;
+}
+
+}  // namespace rfsn
+
+
+
+using namespace rfsn;
+
+struct rfsn_arena {
+    void* k;
+    void* v;
+    int dtype;
+    int groups;
+    int rows;
+    int head_dim;
+    int device;
+    bool has_tma;
+    CUtensorMap maps[4];  // K 64-row box, V 64-row box, K 8-row box, V 8-row box
+};
+
+namespace {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess) {
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+        }
+    }
+    return fn;
+}
+
+rfsn_status encode_map(CUtensorMap* map, void* base, int dtype, int groups, int rows, int head_dim, int box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (fn == nullptr) {
+        set_error("cuTensorMapEncodeTiled is not available from the CUDA driver");
+        return RFSN_ERR_CUDA;
+    }
+    const int es = dtype_size(dtype);
+    cuuint64_t gdim[2] = {(cuuint64_t)head_dim, (cuuint64_t)groups * (cuuint64_t)rows};
+    cuuint64_t gstride[1] = {(cuuint64_t)head_dim * es};
+    cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+    cuuint32_t estride[2] = {1, 1};
+    CUresult r = fn(map, dtype == RFSN_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base,
+                    gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("cuTensorMapEncodeTiled failed with CUresult %d", (int)r);
+        return RFSN_ERR_CUDA;
+    }
+    return RFSN_OK;
+}
+
+int sm_count_cached() {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    static int cache[64] = {0};
+    if (dev < 0 || dev >= 64) return 148;
+    if (cache[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        cache[dev] = n;
+    }
+    return cache[dev];
+}
+
+bool valid_dtype(int dt) { return dt == RFSN_F32 || dt == RFSN_F16 || dt == RFSN_BF16; }
+
+// Split-KV sizing: `target` CTAs in total, at most max_splits per group, at
+// least one tile per split; returns splits and tiles per split.
+void choose_splits(int total_tiles, int groups_x_qblocks, int target, int max_splits, int* splits, int* tps) {
+    int s = target / (groups_x_qblocks > 0 ? groups_x_qblocks : 1);
+    if (s < 1) s = 1;
+    if (s > max_splits) s = max_splits;
+    if (s > total_tiles) s = total_tiles;
+    if (s < 1) s = 1;
+    int per = (total_tiles + s - 1) / s;
+    if (per < 1) per = 1;
+    *tps = per;
+    *splits = (total_tiles + per - 1) / per;
+    if (*splits < 1) *splits = 1;
+}
+
+constexpr int kFastStages = 3;
+constexpr int kFastCtasPerSm = 2;
+constexpr int kGenericMaxSplits = 256;
+
+int generic_max_splits(int head_dim) {
+    // finish_splits scratch in the generic kernel lives in the staged-key buffer.
+    const int avail = 32 * (head_dim + 1) + 32 * head_dim;
+    int m = avail / 8 - 2;
+    return m < kGenericMaxSplits ? m : kGenericMaxSplits;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* rfsn_last_error(void) { return g_last_error.c_str(); }
+
+int rfsn_abi_version(void) { return RFSN_ABI_VERSION; }
+
+uint64_t rfsn_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+rfsn_status rfsn_device_sm_count(int* out) {
+    RFSN_CHECK_ARG(out != nullptr, "rfsn_device_sm_count: out is NULL");
+    int dev = 0;
+    RFSN_CUDA(cudaGetDevice(&dev));
+    RFSN_CUDA(cudaDeviceGetAttribute(out, cudaDevAttrMultiProcessorCount, dev));
+    return RFSN_OK;
+}
+
+rfsn_status rfsn_arena_create(void* k_arena, void* v_arena, int dtype, int batch_kv_heads, int rows, int head_dim,
+                              rfsn_arena** out) {
+    RFSN_CHECK_ARG(out != nullptr, "rfsn_arena_create: out is NULL");
+    RFSN_CHECK_ARG(k_arena != nullptr && v_arena != nullptr, "rfsn_arena_create: NULL arena pointer");
+    RFSN_CHECK_ARG(valid_dtype(dtype), "rfsn_arena_create: unknown dtype %d", dtype);
+    RFSN_CHECK_ARG(batch_kv_heads > 0 && rows > 0 && head_dim > 0, "rfsn_arena_create: non-positive shape");
+    RFSN_CHECK_ARG(head_dim % 2 == 0, "rfsn_arena_create: head_dim must be even (RoPE pairs), got %d", head_dim);
+    RFSN_CHECK_ARG((uintptr_t)k_arena % 16 == 0 && (uintptr_t)v_arena % 16 == 0,
+                   "rfsn_arena_create: arena pointers must be 16-byte aligned");
+    rfsn_arena* a = new rfsn_arena();
+    a->k = k_arena;
+    a->v = v_arena;
+    a->dtype = dtype;
+    a->groups = batch_kv_heads;
+    a->rows = rows;
+    a->head_dim = head_dim;
+    cudaGetDevice(&a->device);
+    a->has_tma = false;
+    if ((dtype == RFSN_BF16 || dtype == RFSN_F16) && head_dim == 128) {
+        rfsn_status st = encode_map(&a->maps[0], k_arena, dtype, batch_kv_heads, rows, head_dim, 64);
+        if (st == RFSN_OK) st = encode_map(&a->maps[1], v_arena, dtype, batch_kv_heads, rows, head_dim, 64);
+        if (st == RFSN_OK) st = encode_map(&a->maps[2], k_arena, dtype, batch_kv_heads, rows, head_dim, 8);
+        if (st == RFSN_OK) st = encode_map(&a->maps[3], v_arena, dtype, batch_kv_heads, rows, head_dim, 8);
+        if (st != RFSN_OK) {
+            delete a;
+            return st;
+        }
+        a->has_tma = true;
+    }
+    *out = a;
+    return RFSN_OK;
+}
+
+rfsn_status rfsn_arena_destroy(rfsn_arena* arena) {
+    delete arena;
+    return RFSN_OK;
+}
+
+rfsn_status rfsn_rope_append(const void* q, const void* k, const void* v, int in_dtype, const float* inv_freq, int pos0,
+                             int batch, int q_heads, int kv_heads, int len, int head_dim, float* q_out,
+                             const rfsn_arena* arena, int ring_row0, int capacity, int write_index, void* stream) {
+    RFSN_CHECK_ARG(arena != nullptr, "rfsn_rope_append: NULL arena");
+    RFSN_CHECK_ARG((k != nullptr) == (v != nullptr), "rfsn_rope_append: k and v must both be given or both NULL");
+    if (k == nullptr) {
+        RFSN_CHECK_ARG(q != nullptr && q_out != nullptr && inv_freq != nullptr,
+                       "rfsn_rope_append: rotating q alone needs q, q_out and inv_freq");
+        kv_heads = 0;
+    }
+    RFSN_CHECK_ARG(valid_dtype(in_dtype), "rfsn_rope_append: unknown dtype %d", in_dtype);
+    RFSN_CHECK_ARG(in_dtype == arena->dtype, "rfsn_rope_append: input dtype %d differs from cache dtype %d", in_dtype,
+                   arena->dtype);
+    RFSN_CHECK_ARG(batch > 0 && kv_heads >= 0 && len > 0 && q_heads >= 0, "rfsn_rope_append: non-positive shape");
+    RFSN_CHECK_ARG(head_dim == arena->head_dim, "rfsn_rope_append: head_dim %d != arena head_dim %d", head_dim,
+                   arena->head_dim);
+    RFSN_CHECK_ARG(k == nullptr || batch * kv_heads == arena->groups,
+                   "rfsn_rope_append: batch*kv_heads %d != arena groups %d", batch * kv_heads, arena->groups);
+    RFSN_CHECK_ARG(capacity > 0 && ring_row0 >= 0 && ring_row0 + capacity <= arena->rows,
+                   "rfsn_rope_append: ring rows [%d, %d) outside the arena (%d rows)", ring_row0, ring_row0 + capacity,
+                   arena->rows);
+    RFSN_CHECK_ARG(write_index >= 0 && write_index < capacity, "rfsn_rope_append: write_index %d outside [0, %d)",
+                   write_index, capacity);
+    if (len > capacity) {
+        set_error("append_exact: chunk of %d tokens exceeds the ring capacity %d", len, capacity);
+        return RFSN_ERR_OVERFLOW;
+    }
+    const int qh = (inv_freq != nullptr && q != nullptr) ? q_heads : 0;
+    return rope_append_launch(in_dtype, q, k, v, inv_freq, pos0, batch, qh, kv_heads, len, head_dim, q_out, arena->k,
+                              arena->v, arena->rows, ring_row0, capacity, write_index, static_cast<cudaStream_t>(stream));
+}
+
+rfsn_status rfsn_arena_copy_rows(const rfsn_arena* arena, int src_row0, int src_offset, int src_wrap, int dst_row0,
+                                 int count, void* stream) {
+    RFSN_CHECK_ARG(arena != nullptr, "rfsn_arena_copy_rows: NULL arena");
+    RFSN_CHECK_ARG(count >= 0, "rfsn_arena_copy_rows: negative count");
+    if (count == 0) return RFSN_OK;
+    RFSN_CHECK_ARG(src_wrap >= 0 && src_offset >= 0, "rfsn_arena_copy_rows: negative offset/wrap");
+    const int src_span = src_wrap > 0 ? src_wrap : src_offset + count;
+    RFSN_CHECK_ARG(src_row0 >= 0 && src_row0 + src_span <= arena->rows, "rfsn_arena_copy_rows: source rows outside the arena");
+    RFSN_CHECK_ARG(src_wrap == 0 || (src_offset < src_wrap && count <= src_wrap),
+                   "rfsn_arena_copy_rows: wrapped source range larger than the ring");
+    RFSN_CHECK_ARG(dst_row0 >= 0 && dst_row0 + count <= arena->rows, "rfsn_arena_copy_rows: destination rows outside the arena");
+    const int row_bytes = arena->head_dim * dtype_size(arena->dtype);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (row_bytes % 16 == 0) {
+        return copy_rows_launch(arena->k, arena->v, arena->groups, arena->rows, row_bytes, src_row0, src_offset,
+                                src_wrap, dst_row0, count, s);
+    }
+    // Rows not a multiple of 16 bytes: per-piece 2-D copies (at most two pieces when wrapping).
+    const size_t pitch = (size_t)arena->rows * row_bytes;
+    int done = 0;
+    while (done < count) {
+        int srow = src_offset + done;
+        if (src_wrap > 0) srow %= src_wrap;
+        int n = count - done;
+        if (src_wrap > 0 && srow + n > src_wrap) n = src_wrap - srow;
+        for (int t = 0; t < 2; ++t) {
+            uint8_t* base = static_cast<uint8_t*>(t == 0 ? arena->k : arena->v);
+            RFSN_CUDA(cudaMemcpy2DAsync(base + (size_t)(dst_row0 + done) * row_bytes, pitch,
+                                        base + (size_t)(src_row0 + srow) * row_bytes, pitch, (size_t)n * row_bytes,
+                                        arena->groups, cudaMemcpyDeviceToDevice, s));
+        }
+        done += n;
+    }
+    return RFSN_OK;
+}
+
+static rfsn_status block_xfer(const rfsn_arena* arena, int row0, int count, const void* k_host, const void* v_host,
+                              void* k_out, void* v_out, void* stream, void* done_event, bool upload) {
+    RFSN_CHECK_ARG(arena != nullptr, "block transfer: NULL arena");
+    RFSN_CHECK_ARG(count > 0 && row0 >= 0 && row0 + count <= arena->rows, "block transfer: rows [%d, %d) outside the arena",
+                   row0, row0 + count);
+    const size_t row_bytes = (size_t)arena->head_dim * dtype_size(arena->dtype);
+    const size_t pitch = (size_t)arena->rows * row_bytes;
+    const size_t blk_pitch = (size_t)count * row_bytes;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    for (int t = 0; t < 2; ++t) {
+        uint8_t* base = static_cast<uint8_t*>(t == 0 ? arena->k : arena->v) + (size_t)row0 * row_bytes;
+        if (upload) {
+            const void* src = t == 0 ? k_host : v_host;
+            RFSN_CHECK_ARG(src != nullptr, "rfsn_block_upload: NULL source");
+            RFSN_CUDA(cudaMemcpy2DAsync(base, pitch, src, blk_pitch, blk_pitch, arena->groups, cudaMemcpyDefault, s));
+        } else {
+            void* dst = t == 0 ? k_out : v_out;
+            RFSN_CHECK_ARG(dst != nullptr, "rfsn_block_download: NULL destination");
+            RFSN_CUDA(cudaMemcpy2DAsync(dst, blk_pitch, base, pitch, blk_pitch, arena->groups, cudaMemcpyDefault, s));
+        }
+    }
+    if (done_event != nullptr) RFSN_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(done_event), s));
+    return RFSN_OK;
+}
+
+rfsn_status rfsn_block_upload(const rfsn_arena* arena, int dst_row0, int count, const void* k_src, const void* v_src,
+                              void* stream, void* done_event) {
+    return block_xfer(arena, dst_row0, count, k_src, v_src, nullptr, nullptr, stream, done_event, true);
+}
+
+rfsn_status rfsn_block_download(const rfsn_arena* arena, int src_row0, int count, void* k_dst, void* v_dst, void* stream,
+                                void* done_event) {
+    return block_xfer(arena, src_row0, count, nullptr, nullptr, k_dst, v_dst, stream, done_event, false);
+}
+
+rfsn_status rfsn_event_wait(void* event, int64_t timeout_us) {
+    RFSN_CHECK_ARG(event != nullptr, "rfsn_event_wait: NULL event");
+    const auto t0 = std::chrono::steady_clock::now();
+    while (true) {
+        cudaError_t e = cudaEventQuery(static_cast<cudaEvent_t>(event));
+        if (e == cudaSuccess) return RFSN_OK;
+        if (e != cudaErrorNotReady) return cuda_status(e, "cudaEventQuery");
+        const auto us = std::chrono::duration_cast<std::chrono::microseconds>(std::chrono::steady_clock::now() - t0).count();
+        if (us >= timeout_us) {
+            set_error("event not complete after %lld us", (long long)timeout_us);
+            return RFSN_ERR_TIMEOUT;
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+}
+
+rfsn_status rfsn_attention_workspace_size(int batch, int q_heads, int kv_heads, int q_len, int head_dim, int max_splits,
+                                          size_t* bytes) {
+    RFSN_CHECK_ARG(bytes != nullptr, "rfsn_attention_workspace_size: bytes is NULL");
+    RFSN_CHECK_ARG(batch > 0 && q_heads > 0 && kv_heads > 0 && q_len > 0 && head_dim > 0,
+                   "rfsn_attention_workspace_size: non-positive shape");
+    RFSN_CHECK_ARG(q_heads % kv_heads == 0, "num_heads (%d) must be divisible by num_kv_heads (%d)", q_heads, kv_heads);
+    const int G = q_heads / kv_heads;
+    const int nslots = q_len * G;
+    const int slots_ws = nslots < 4 ? 4 : nslots;
+    const int qblocks = (nslots + 7) / 8;
+    const int splits = max_splits > 0 ? max_splits : kGenericMaxSplits;
+    *bytes = ws_layout(batch * kv_heads, qblocks, splits, slots_ws, head_dim).total;
+    return RFSN_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+struct CommonArgs {
+    int batch, q_heads, kv_heads, q_len, head_dim, G, nslots, slots_ws, qblocks, groups;
+};
+
+rfsn_status check_common(const float* q, int batch, int q_heads, int kv_heads, int q_len, int head_dim, float* out,
+                         void* workspace, CommonArgs* a) {
+    RFSN_CHECK_ARG(q != nullptr && out != nullptr, "attention: NULL q/out");
+    RFSN_CHECK_ARG(workspace != nullptr, "attention: NULL workspace");
+    RFSN_CHECK_ARG(batch > 0 && q_heads > 0 && kv_heads > 0 && q_len > 0, "attention: non-positive shape");
+    RFSN_CHECK_ARG(q_heads % kv_heads == 0, "num_heads (%d) must be divisible by num_kv_heads (%d)", q_heads, kv_heads);
+    RFSN_CHECK_ARG(head_dim > 0 && head_dim <= 256, "attention: head_dim %d outside [1, 256]", head_dim);
+    a->batch = batch;
+    a->q_heads = q_heads;
+    a->kv_heads = kv_heads;
+    a->q_len = q_len;
+    a->head_dim = head_dim;
+    a->G = q_heads / kv_heads;
+    a->nslots = q_len * a->G;
+    a->slots_ws = a->nslots < 4 ? 4 : a->nslots;
+    a->qblocks = (a->nslots + 7) / 8;
+    a->groups = batch * kv_heads;
+    RFSN_CHECK_ARG((long)a->groups * a->qblocks <= kMaxCounters, "attention: batch*kv_heads*q_blocks above %d",
+                   kMaxCounters);
+    return RFSN_OK;
+}
+
+float qscale_for(int head_dim) {
+    // scale = 1 / sqrt(D) (attention_exact.py:139), times log2(e) for exp2.
+    const float scale = (float)(1.0 / std::sqrt((double)head_dim));
+    return scale * 1.4426950408889634f;
+}
+
+}  // namespace
+
+extern "C" {
+
+rfsn_status rfsn_paged_attention(const rfsn_arena* arena, const float* q, int batch, int q_heads, int kv_heads, int q_len,
+                                 int q_pos0, const rfsn_page_table* table, const rfsn_hot_window* hot, float* out,
+                                 float* lse, void* workspace, size_t workspace_bytes, int max_splits, void* stream) {
+    RFSN_CHECK_ARG(arena != nullptr && table != nullptr && hot != nullptr, "rfsn_paged_attention: NULL arena/table/hot");
+    CommonArgs a;
+    rfsn_status st = check_common(q, batch, q_heads, kv_heads, q_len, arena->head_dim, out, workspace, &a);
+    if (st != RFSN_OK) return st;
+    RFSN_CHECK_ARG(a.groups == arena->groups, "rfsn_paged_attention: batch*kv_heads %d != arena groups %d", a.groups,
+                   arena->groups);
+    RFSN_CHECK_ARG(table->n_blocks >= 0 && (table->n_blocks == 0 || table->records != nullptr),
+                   "rfsn_paged_attention: bad page table");
+    RFSN_CHECK_ARG(hot->length >= 0 && hot->length <= hot->capacity && hot->head_index >= 0 &&
+                       hot->head_index < (hot->capacity > 0 ? hot->capacity : 1) &&
+                       hot->ring_row0 >= 0 && hot->ring_row0 + hot->capacity <= arena->rows,
+                   "rfsn_paged_attention: bad hot window");
+    const int first = hot->length < hot->capacity - hot->head_index ? hot->length : hot->capacity - hot->head_index;
+    const int hot_tiles = (first + kTile - 1) / kTile + (hot->length - first + kTile - 1) / kTile;
+    const int total_tiles = table->archived_tiles + hot_tiles;
+    if (total_tiles <= 0) {
+        set_error("run_segmented_attention requires at least one KV segment");
+        return RFSN_ERR_INVALID_ARG;
+    }
+    const int sms = sm_count_cached();
+    const bool use_fast = arena->has_tma && arena->head_dim == 128 && a.nslots <= 4;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (use_fast) {
+        fast::Params p;
+        int splits, tps;
+        const int cap = max_splits > 0 ? (max_splits < fast_max_splits() ? max_splits : fast_max_splits()) : fast_max_splits();
+        choose_splits(total_tiles, a.groups, sms * kFastCtasPerSm, cap, &splits, &tps);
+        const WsLayout w = ws_layout(a.groups, 1, splits, a.slots_ws, 128);
+        if (w.total > workspace_bytes) {
+            set_error("attention workspace too small: need %zu bytes, have %zu", w.total, workspace_bytes);
+            return RFSN_ERR_OVERFLOW;
+        }
+        p.q = q;
+        p.out = out;
+        p.lse = lse;
+        p.records = reinterpret_cast<const int4*>(table->records);
+        p.n_blocks = table->n_blocks;
+        p.archived_tiles = table->archived_tiles;
+        p.ring_row0 = hot->ring_row0;
+        p.capacity = hot->capacity;
+        p.head = hot->head_index;
+        p.hlen = hot->length;
+        p.hstart = hot->start_pos;
+        p.rows = arena->rows;
+        p.q_heads = q_heads;
+        p.kv_heads = kv_heads;
+        p.q_len = q_len;
+        p.q_pos0 = q_pos0;
+        p.groups_per_kv = a.G;
+        p.nslots = a.nslots;
+        p.total_tiles = total_tiles;
+        p.tiles_per_split = tps;
+        p.splits = splits;
+        p.groups = a.groups;
+        p.qscale = qscale_for(128);
+        p.pscale = arena->dtype == RFSN_F16 ? 4096.f : 1.f;
+        p.ws = ws_view(workspace, w);
+        return fast_launch(arena->dtype, arena->maps, p, kFastStages, s);
+    }
+    generic::Params p;
+    memset(&p, 0, sizeof(p));
+    int splits, tps;
+    int cap = generic_max_splits(arena->head_dim);
+    if (max_splits > 0 && max_splits < cap) cap = max_splits;
+    choose_splits(total_tiles, a.groups * a.qblocks, sms * 4, cap, &splits, &tps);
+    const WsLayout w = ws_layout(a.groups, a.qblocks, splits, a.slots_ws, arena->head_dim);
+    if (w.total > workspace_bytes) {
+        set_error("attention workspace too small: need %zu bytes, have %zu", w.total, workspace_bytes);
+        return RFSN_ERR_OVERFLOW;
+    }
+    p.q = q;
+    p.out = out;
+    p.lse = lse;
+    p.head_dim = arena->head_dim;
+    p.q_heads = q_heads;
+    p.kv_heads = kv_heads;
+    p.q_len = q_len;
+    p.q_pos0 = q_pos0;
+    p.groups_per_kv = a.G;
+    p.nslots_total = a.nslots;
+    p.slots_ws = a.slots_ws;
+    p.total_tiles = total_tiles;
+    p.tiles_per_split = tps;
+    p.splits = splits;
+    p.qblocks = a.qblocks;
+    p.qscale = qscale_for(arena->head_dim);
+    p.ws = ws_view(workspace, w);
+    p.arena_k = arena->k;
+    p.arena_v = arena->v;
+    p.rows = arena->rows;
+    p.records = reinterpret_cast<const int4*>(table->records);
+    p.n_blocks = table->n_blocks;
+    p.archived_tiles = table->archived_tiles;
+    p.ring_row0 = hot->ring_row0;
+    p.capacity = hot->capacity;
+    p.head = hot->head_index;
+    p.hlen = hot->length;
+    p.hstart = hot->start_pos;
+    return generic_launch(arena->dtype, true, p, a.groups, s);
+}
+
+rfsn_status rfsn_segmented_attention(const float* q, int batch, int q_heads, int kv_heads, int q_len, int q_pos0,
+                                     int head_dim, int kv_dtype, const rfsn_segment_desc* segments, int n_segments,
+                                     int total_tiles, float* out, float* lse, void* workspace, size_t workspace_bytes,
+                                     int max_splits, void* stream) {
+    CommonArgs a;
+    rfsn_status st = check_common(q, batch, q_heads, kv_heads, q_len, head_dim, out, workspace, &a);
+    if (st != RFSN_OK) return st;
+    RFSN_CHECK_ARG(valid_dtype(kv_dtype), "rfsn_segmented_attention: unknown dtype %d", kv_dtype);
+    if (n_segments <= 0 || total_tiles <= 0) {
+        set_error("run_segmented_attention requires at least one KV segment");
+        return RFSN_ERR_INVALID_ARG;
+    }
+    RFSN_CHECK_ARG(segments != nullptr, "rfsn_segmented_attention: NULL segment table");
+    generic::Params p;
+    memset(&p, 0, sizeof(p));
+    int splits, tps;
+    int cap = generic_max_splits(head_dim);
+    if (max_splits > 0 && max_splits < cap) cap = max_splits;
+    choose_splits(total_tiles, a.groups * a.qblocks, sm_count_cached() * 4, cap, &splits, &tps);
+    const WsLayout w = ws_layout(a.groups, a.qblocks, splits, a.slots_ws, head_dim);
+    if (w.total > workspace_bytes) {
+        set_error("attention workspace too small: need %zu bytes, have %zu", w.total, workspace_bytes);
+        return RFSN_ERR_OVERFLOW;
+    }
+    p.q = q;
+    p.out = out;
+    p.lse = lse;
+    p.head_dim = head_dim;
+    p.q_heads = q_heads;
+    p.kv_heads = kv_heads;
+    p.q_len = q_len;
+    p.q_pos0 = q_pos0;
+    p.groups_per_kv = a.G;
+    p.nslots_total = a.nslots;
+    p.slots_ws = a.slots_ws;
+    p.total_tiles = total_tiles;
+    p.tiles_per_split = tps;
+    p.splits = splits;
+    p.qblocks = a.qblocks;
+    p.qscale = qscale_for(head_dim);
+    p.ws = ws_view(workspace, w);
+    p.segs = segments;
+    p.n_segs = n_segments;
+    return generic_launch(kv_dtype, false, p, a.groups, static_cast<cudaStream_t>(stream));
+}
+
+rfsn_status rfsn_lse_merge(const float* parts_out, const float* parts_lse, int n_parts, int rows, int head_dim,
+                           float* out, float* lse_out, void* stream) {
+    RFSN_CHECK_ARG(parts_out != nullptr && parts_lse != nullptr && out != nullptr, "rfsn_lse_merge: NULL pointer");
+    RFSN_CHECK_ARG(n_parts > 0 && rows > 0 && head_dim > 0, "rfsn_lse_merge: non-positive shape");
+    return lse_merge_launch(parts_out, parts_lse, n_parts, rows, head_dim, out, lse_out, static_cast<cudaStream_t>(stream));
+}
+
+rfsn_status rfsn_workspace_check(void* workspace, void* stream, int64_t timeout_us) {
+    RFSN_CHECK_ARG(workspace != nullptr, "rfsn_workspace_check: NULL workspace");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaEvent_t ev;
+    RFSN_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+    cudaError_t e = cudaEventRecord(ev, s);
+    if (e != cudaSuccess) {
+        cudaEventDestroy(ev);
+        return cuda_status(e, "cudaEventRecord");
+    }
+    rfsn_status st = rfsn_event_wait(ev, timeout_us);
+    cudaEventDestroy(ev);
+    if (st != RFSN_OK) return st;
+    int word = 0;
+    RFSN_CUDA(cudaMemcpy(&word, workspace, sizeof(int), cudaMemcpyDeviceToHost));
+    if (word != 0) {
+        const int zero = 0;
+        RFSN_CUDA(cudaMemcpy(workspace, &zero, sizeof(int), cudaMemcpyHostToDevice));
+        set_error("attention kernel reported device error %d (bounded wait expired)", word);
+        return RFSN_ERR_DEVICE;
+    }
+    return RFSN_OK;
+}
+
+}  // extern "C"

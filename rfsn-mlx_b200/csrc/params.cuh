@@ -1,0 +1,62 @@
+// Kernel parameter blocks and host launchers shared between the kernel
+// translation units and the C ABI layer (capi.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace rfsn {
+namespace fast {
+struct Params {
+    const float* q;
+    float* out;
+    float* lse;
+    const int4* records;
+    int n_blocks, archived_tiles;
+    int ring_row0, capacity, head, hlen, hstart;
+    int rows;                 // arena rows per head
+    int q_heads, kv_heads, q_len, q_pos0, groups_per_kv, nslots;
+    int total_tiles, tiles_per_split, splits, groups;
+    float qscale;             // 1/sqrt(D) * log2(e)
+    float pscale;             // power-of-two scale applied to p before the 16-bit split
+    WsView ws;
+};
+}  // namespace fast
+
+namespace generic {
+struct Params {
+    const float* q;
+    float* out;
+    float* lse;
+    int head_dim, q_heads, kv_heads, q_len, q_pos0, groups_per_kv, nslots_total, slots_ws;
+    int total_tiles, tiles_per_split, splits, qblocks;
+    float qscale;
+    WsView ws;
+    // paged mode
+    const void* arena_k;
+    const void* arena_v;
+    int rows;
+    const int4* records;
+    int n_blocks, archived_tiles;
+    int ring_row0, capacity, head, hlen, hstart;
+    // segment-list mode
+    const rfsn_segment_desc* segs;
+    int n_segs;
+};
+}  // namespace generic
+
+// decode_attn.cu
+int fast_max_splits();
+rfsn_status fast_launch(int dtype, const CUtensorMap* maps, const fast::Params& p, int stages, cudaStream_t stream);
+// generic_attn.cu
+rfsn_status generic_launch(int dtype, bool paged, const generic::Params& p, int groups, cudaStream_t stream);
+// merge.cu
+rfsn_status lse_merge_launch(const float* parts_out, const float* parts_lse, int n_parts, int rows, int head_dim,
+                             float* out, float* lse_out, cudaStream_t stream);
+// ring.cu
+rfsn_status rope_append_launch(int dtype, const void* q, const void* k, const void* v, const float* inv_freq, int pos0,
+                               int batch, int q_heads, int kv_heads, int len, int head_dim, float* q_out, void* ak,
+                               void* av, int rows, int ring_row0, int capacity, int write_index, cudaStream_t stream);
+rfsn_status copy_rows_launch(void* ak, void* av, int groups, int rows, int row_bytes, int src_row0, int src_offset,
+                             int src_wrap, int dst_row0, int count, cudaStream_t stream);
+
+}  // namespace rfsn

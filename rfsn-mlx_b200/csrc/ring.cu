@@ -1,0 +1,125 @@
+// Hot-ring kernels: fused RoPE + append, and arena row copies (seal).
+#include "params.cuh"
+
+namespace rfsn {
+namespace ring {
+
+// One thread per (tensor row, rotation pair j): rotates x[j], x[j + half]
+// exactly as layer.py:38-51 with the float32 tables of layer.py:20-35:
+//   f = pos * inv_freq[j]                (one float32 product)
+//   out[j]        = x1 * cos f - x2 * sin f
+//   out[j + half] = x1 * sin f + x2 * cos f
+// Products and sums are rounded separately (no FMA contraction) like the
+// reference's elementwise ops; cosf/sinf are the accurate CUDA versions.
+template <typename TIn, typename TCache>
+__global__ void rope_append_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k, const TIn* __restrict__ v,
+                                   const float* __restrict__ inv_freq, int pos0, int batch, int q_heads, int kv_heads,
+                                   int len, int head_dim, float* __restrict__ q_out, TCache* __restrict__ ak,
+                                   TCache* __restrict__ av, int rows, int ring_row0, int capacity, int write_index) {
+    const int half = head_dim >> 1;
+    const long q_rows = (long)batch * q_heads * len;
+    const long kv_rows = (long)batch * kv_heads * len;
+    const long total = (q_rows + kv_rows) * half;
+    for (long idx = blockIdx.x * (long)blockDim.x + threadIdx.x; idx < total; idx += (long)gridDim.x * blockDim.x) {
+        const long r = idx / half;
+        const int j = (int)(idx - r * half);
+        const bool is_q = r < q_rows;
+        const long rr = is_q ? r : r - q_rows;
+        const int l = (int)(rr % len);
+        float x1, x2;
+        if (is_q) {
+            x1 = to_f32<TIn>(q[rr * head_dim + j]);
+            x2 = to_f32<TIn>(q[rr * head_dim + j + half]);
+        } else {
+            x1 = to_f32<TIn>(k[rr * head_dim + j]);
+            x2 = to_f32<TIn>(k[rr * head_dim + j + half]);
+        }
+        float o1 = x1, o2 = x2;
+        if (inv_freq != nullptr) {
+            const float f = __fmul_rn((float)(pos0 + l), inv_freq[j]);
+            const float c = cosf(f), s = sinf(f);
+            o1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+            o2 = __fadd_rn(__fmul_rn(x1, s), __fmul_rn(x2, c));
+        }
+        if (is_q) {
+            if (q_out != nullptr) {
+                q_out[rr * head_dim + j] = o1;
+                q_out[rr * head_dim + j + half] = o2;
+            }
+        } else {
+            // rr = (b * kv_heads + h) * len + l  ->  arena row of the ring slot
+            const long bh = rr / len;
+            const int slot = (write_index + l) % capacity;
+            const long dst = (bh * rows + ring_row0 + slot) * head_dim;
+            ak[dst + j] = from_f32<TCache>(o1);
+            ak[dst + j + half] = from_f32<TCache>(o2);
+            av[dst + j] = from_f32<TCache>(to_f32<TIn>(v[rr * head_dim + j]));
+            av[dst + j + half] = from_f32<TCache>(to_f32<TIn>(v[rr * head_dim + j + half]));
+        }
+    }
+}
+
+// Copy `count` rows of every head from src (read modulo src_wrap when > 0)
+// to dst, 16 bytes per thread step, for K and V. Source and destination
+// row ranges must not overlap (seal copies ring rows into block rows).
+__global__ void copy_rows_kernel(uint8_t* __restrict__ ak, uint8_t* __restrict__ av, int groups, int rows,
+                                 int row_bytes, int src_row0, int src_offset, int src_wrap, int dst_row0, int count) {
+    const int vec_per_row = row_bytes / 16;
+    const long total = (long)groups * count * vec_per_row;
+    for (long idx = blockIdx.x * (long)blockDim.x + threadIdx.x; idx < total; idx += (long)gridDim.x * blockDim.x) {
+        const int vi = (int)(idx % vec_per_row);
+        const long rr = idx / vec_per_row;
+        const int i = (int)(rr % count);
+        const long gidx = rr / count;
+        int s = src_offset + i;
+        if (src_wrap > 0) s %= src_wrap;
+        const long src = ((gidx * rows + src_row0 + s) * row_bytes) + vi * 16;
+        const long dst = ((gidx * rows + dst_row0 + i) * row_bytes) + vi * 16;
+        *reinterpret_cast<uint4*>(ak + dst) = *reinterpret_cast<const uint4*>(ak + src);
+        *reinterpret_cast<uint4*>(av + dst) = *reinterpret_cast<const uint4*>(av + src);
+    }
+}
+
+}  // namespace ring
+
+rfsn_status rope_append_launch(int dtype, const void* q, const void* k, const void* v, const float* inv_freq, int pos0,
+                               int batch, int q_heads, int kv_heads, int len, int head_dim, float* q_out, void* ak,
+                               void* av, int rows, int ring_row0, int capacity, int write_index, cudaStream_t stream) {
+    const long total = ((long)batch * (q_heads + kv_heads) * len) * (head_dim / 2);
+    const int threads = 256;
+    long blocks = (total + threads - 1) / threads;
+    if (blocks > 65535L * 8) blocks = 65535L * 8;
+    if (blocks < 1) blocks = 1;
+#define RFSN_ROPE_LAUNCH(T)                                                                                     \
+    ring::rope_append_kernel<T, T><<<(unsigned)blocks, threads, 0, stream>>>(                                   \
+        static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(v), inv_freq, pos0, batch,    \
+        q_heads, kv_heads, len, head_dim, q_out, static_cast<T*>(ak), static_cast<T*>(av), rows, ring_row0,     \
+        capacity, write_index)
+    if (dtype == RFSN_F32) {
+        RFSN_ROPE_LAUNCH(float);
+    } else if (dtype == RFSN_F16) {
+        RFSN_ROPE_LAUNCH(__half);
+    } else {
+        RFSN_ROPE_LAUNCH(__nv_bfloat16);
+    }
+#undef RFSN_ROPE_LAUNCH
+    RFSN_CUDA(cudaGetLastError());
+    note_launch();
+    return RFSN_OK;
+}
+
+rfsn_status copy_rows_launch(void* ak, void* av, int groups, int rows, int row_bytes, int src_row0, int src_offset,
+                             int src_wrap, int dst_row0, int count, cudaStream_t stream) {
+    const long total = (long)groups * count * (row_bytes / 16);
+    long blocks = (total + 255) / 256;
+    if (blocks > 65535L * 4) blocks = 65535L * 4;
+    if (blocks < 1) blocks = 1;
+    ring::copy_rows_kernel<<<(unsigned)blocks, 256, 0, stream>>>(static_cast<uint8_t*>(ak), static_cast<uint8_t*>(av),
+                                                                  groups, rows, row_bytes, src_row0, src_offset,
+                                                                  src_wrap, dst_row0, count);
+    RFSN_CUDA(cudaGetLastError());
+    note_launch();
+    return RFSN_OK;
+}
+
+}  // namespace rfsn

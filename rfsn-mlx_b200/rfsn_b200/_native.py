@@ -1,0 +1,272 @@
+"""ctypes binding of the C ABI in ``include/rfsn_b200.h``.
+
+This is the only module that talks to ``librfsn_b200.so``. Tensors cross the
+boundary as raw device pointers (``tensor.data_ptr()``) plus sizes; streams as
+``torch.cuda.current_stream().cuda_stream``. Status codes become the exception
+types the reference raises for the same condition (ValueError for bad
+arguments, RuntimeError for overflow / device failures, TimeoutError for an
+expired bounded wait).
+
+There is no CPU fallback: if the library or a CUDA device is missing, every
+compute call raises ``NativeUnavailable``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+from typing import Optional
+
+import torch
+
+_LIB_NAME = "librfsn_b200.so"
+_LIB_PATH = Path(__file__).resolve().parent / _LIB_NAME
+
+RFSN_OK = 0
+RFSN_ERR_INVALID_ARG = 1
+RFSN_ERR_UNSUPPORTED = 2
+RFSN_ERR_OVERFLOW = 3
+RFSN_ERR_TIMEOUT = 4
+RFSN_ERR_CUDA = 5
+RFSN_ERR_DEVICE = 6
+
+RFSN_F32 = 0
+RFSN_F16 = 1
+RFSN_BF16 = 2
+TILE_KEYS = 64
+
+DTYPE_CODE = {torch.float32: RFSN_F32, torch.float16: RFSN_F16, torch.bfloat16: RFSN_BF16}
+
+# Every symbol declared in include/rfsn_b200.h.
+EXPORTED_SYMBOLS = (
+    "rfsn_last_error",
+    "rfsn_abi_version",
+    "rfsn_device_sm_count",
+    "rfsn_arena_create",
+    "rfsn_arena_destroy",
+    "rfsn_rope_append",
+    "rfsn_arena_copy_rows",
+    "rfsn_block_upload",
+    "rfsn_block_download",
+    "rfsn_event_wait",
+    "rfsn_attention_workspace_size",
+    "rfsn_paged_attention",
+    "rfsn_segmented_attention",
+    "rfsn_lse_merge",
+    "rfsn_workspace_check",
+    "rfsn_launch_count",
+)
+
+
+class NativeUnavailable(RuntimeError):
+    """The CUDA library or device needed by the B200 path is not available."""
+
+
+class PageTableC(ctypes.Structure):
+    _fields_ = [
+        ("records", ctypes.c_void_p),
+        ("n_blocks", ctypes.c_int32),
+        ("archived_tokens", ctypes.c_int32),
+        ("archived_tiles", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+    ]
+
+
+class HotWindowC(ctypes.Structure):
+    _fields_ = [
+        ("ring_row0", ctypes.c_int32),
+        ("capacity", ctypes.c_int32),
+        ("head_index", ctypes.c_int32),
+        ("length", ctypes.c_int32),
+        ("start_pos", ctypes.c_int32),
+        ("reserved", ctypes.c_int32 * 3),
+    ]
+
+
+class SegmentDescC(ctypes.Structure):
+    _fields_ = [
+        ("k_ptr", ctypes.c_uint64),
+        ("v_ptr", ctypes.c_uint64),
+        ("k_stride_b", ctypes.c_int64),
+        ("k_stride_h", ctypes.c_int64),
+        ("k_stride_t", ctypes.c_int64),
+        ("v_stride_b", ctypes.c_int64),
+        ("v_stride_h", ctypes.c_int64),
+        ("v_stride_t", ctypes.c_int64),
+        ("pos", ctypes.c_int32),
+        ("len", ctypes.c_int32),
+        ("tile_begin", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+    ]
+
+
+_lib: Optional[ctypes.CDLL] = None
+
+
+def library_path() -> Path:
+    return Path(os.environ.get("RFSN_B200_LIB", str(_LIB_PATH)))
+
+
+def load_library() -> ctypes.CDLL:
+    """Load the shared library (no CUDA device needed just to load it)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    path = library_path()
+    if not path.exists():
+        raise NativeUnavailable(
+            f"{path} is missing; build it with `make -C rfsn-mlx_b200/csrc` (or __graft_entry__.build())"
+        )
+    lib = ctypes.CDLL(str(path))
+    vp, i32, i64, sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t
+    sig = {
+        "rfsn_last_error": (ctypes.c_char_p, []),
+        "rfsn_abi_version": (i32, []),
+        "rfsn_device_sm_count": (i32, [ctypes.POINTER(i32)]),
+        "rfsn_arena_create": (i32, [vp, vp, i32, i32, i32, i32, ctypes.POINTER(vp)]),
+        "rfsn_arena_destroy": (i32, [vp]),
+        "rfsn_rope_append": (i32, [vp, vp, vp, i32, vp, i32, i32, i32, i32, i32, i32, vp, vp, i32, i32, i32, vp]),
+        "rfsn_arena_copy_rows": (i32, [vp, i32, i32, i32, i32, i32, vp]),
+        "rfsn_block_upload": (i32, [vp, i32, i32, vp, vp, vp, vp]),
+        "rfsn_block_download": (i32, [vp, i32, i32, vp, vp, vp, vp]),
+        "rfsn_event_wait": (i32, [vp, i64]),
+        "rfsn_attention_workspace_size": (i32, [i32, i32, i32, i32, i32, i32, ctypes.POINTER(sz)]),
+        "rfsn_paged_attention": (
+            i32,
+            [vp, vp, i32, i32, i32, i32, i32, ctypes.POINTER(PageTableC), ctypes.POINTER(HotWindowC), vp, vp, vp, sz, i32, vp],
+        ),
+        "rfsn_segmented_attention": (
+            i32,
+            [vp, i32, i32, i32, i32, i32, i32, i32, vp, i32, i32, vp, vp, vp, sz, i32, vp],
+        ),
+        "rfsn_lse_merge": (i32, [vp, vp, i32, i32, i32, vp, vp, vp]),
+        "rfsn_workspace_check": (i32, [vp, vp, i64]),
+        "rfsn_launch_count": (ctypes.c_uint64, []),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def lib() -> ctypes.CDLL:
+    lib_ = load_library()
+    if not torch.cuda.is_available():
+        raise NativeUnavailable("the B200 attention path needs a CUDA device; none is visible")
+    return lib_
+
+
+def launch_count() -> int:
+    """Kernels launched by the native library so far in this process."""
+    return int(load_library().rfsn_launch_count())
+
+
+def last_error() -> str:
+    return load_library().rfsn_last_error().decode("utf-8", "replace")
+
+
+def check(status: int, what: str) -> None:
+    if status == RFSN_OK:
+        return
+    msg = last_error()
+    if status == RFSN_ERR_INVALID_ARG:
+        raise ValueError(f"{what}: {msg}")
+    if status == RFSN_ERR_TIMEOUT:
+        raise TimeoutError(f"{what}: {msg}")
+    if status == RFSN_ERR_UNSUPPORTED:
+        raise NotImplementedError(f"{what}: {msg}")
+    raise RuntimeError(f"{what}: {msg}")
+
+
+def stream_ptr(stream: Optional[torch.cuda.Stream] = None) -> int:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return int(s.cuda_stream)
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    try:
+        return DTYPE_CODE[dtype]
+    except KeyError as exc:
+        raise ValueError(f"unsupported dtype {dtype}") from exc
+
+
+class Arena:
+    """Owns the native descriptor (incl. TMA maps) of one layer's K/V arena."""
+
+    def __init__(self, k: torch.Tensor, v: torch.Tensor) -> None:
+        if k.shape != v.shape or k.dtype != v.dtype or k.dim() != 3:
+            raise ValueError("arena K/V must be matching [groups, rows, head_dim] tensors")
+        if not (k.is_cuda and k.is_contiguous() and v.is_contiguous()):
+            raise ValueError("arena K/V must be contiguous CUDA tensors")
+        self.k, self.v = k, v
+        self.groups, self.rows, self.head_dim = (int(x) for x in k.shape)
+        self.dtype = k.dtype
+        handle = ctypes.c_void_p()
+        check(
+            lib().rfsn_arena_create(
+                k.data_ptr(), v.data_ptr(), dtype_code(k.dtype), self.groups, self.rows, self.head_dim,
+                ctypes.byref(handle),
+            ),
+            "rfsn_arena_create",
+        )
+        self.handle = handle
+
+    def close(self) -> None:
+        if self.handle:
+            _lib.rfsn_arena_destroy(self.handle)  # type: ignore[union-attr]
+            self.handle = ctypes.c_void_p()
+
+    def __del__(self) -> None:  # pragma: no cover - interpreter shutdown order
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def workspace_bytes(batch: int, q_heads: int, kv_heads: int, q_len: int, head_dim: int, max_splits: int = 0) -> int:
+    out = ctypes.c_size_t()
+    check(
+        load_library().rfsn_attention_workspace_size(batch, q_heads, kv_heads, q_len, head_dim, max_splits, ctypes.byref(out)),
+        "rfsn_attention_workspace_size",
+    )
+    return int(out.value)
+
+
+class Workspace:
+    """Zero-initialised device scratch for the split-KV attention kernels.
+
+    The kernels leave their arrival counters at zero after every call, so a
+    workspace is zeroed once and reused by calls ordered on one stream. It
+    grows when a call needs more room.
+    """
+
+    def __init__(self, device: torch.device) -> None:
+        self.device = device
+        self.buf = torch.zeros(0, dtype=torch.uint8, device=device)
+
+    def get(self, nbytes: int) -> torch.Tensor:
+        if self.buf.numel() < nbytes:
+            self.buf = torch.zeros(max(nbytes, 2 * self.buf.numel()), dtype=torch.uint8, device=self.device)
+        return self.buf
+
+    def check(self, timeout_s: float = 10.0) -> None:
+        if self.buf.numel():
+            check(
+                lib().rfsn_workspace_check(self.buf.data_ptr(), stream_ptr(), int(timeout_s * 1e6)),
+                "rfsn_workspace_check",
+            )
+
+
+_workspaces: dict[int, Workspace] = {}
+
+
+def default_workspace(device: torch.device) -> Workspace:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    ws = _workspaces.get(idx)
+    if ws is None:
+        ws = Workspace(torch.device("cuda", idx))
+        _workspaces[idx] = ws
+    return ws

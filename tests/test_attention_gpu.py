@@ -1,0 +1,171 @@
+"""Parity of the CUDA attention kernels with the oracle (through the C ABI).
+
+Tolerance: max-abs 2e-3 against the float32 oracle (the bar for fp16/bf16
+K/V with float32 accumulation). The paged kernels keep ~16 significand bits of
+q and p, so a tighter 1e-4 guard is also asserted to catch precision loss.
+"""
+
+import ctypes
+
+import numpy as np
+import pytest
+
+from _util import golden_attention_cases, make_layout, run_paged
+from oracle.numerics import from_storage
+from oracle.segmented_attention import merge_partials, run_segmented_attention
+
+pytestmark = pytest.mark.gpu
+ATOL = 2e-3
+GUARD = 1e-4
+
+
+def _q(seed, B, H, Lq, D):
+    return np.random.default_rng(seed).standard_normal((B, H, Lq, D), dtype=np.float32)
+
+
+def _check(layout, q, q_pos0, *, max_splits=0, guard=GUARD):
+    ref, ref_lse = run_segmented_attention(q, layout.oracle_segments(), q_pos0, return_lse=True, grouped=True)
+    out, lse = run_paged(layout, q, q_pos0, max_splits=max_splits)
+    err = float(np.abs(out - ref).max())
+    assert err <= ATOL, err
+    assert err <= guard, err
+    np.testing.assert_allclose(lse, ref_lse, atol=1e-4, rtol=1e-5)
+    return out
+
+
+def test_decode_8k_fp16_full_size():
+    # 24 archived blocks of 256 + a full 2048-token ring; the query is the last token.
+    for head in (0, 777):
+        lay = make_layout("float16", 1, 8, 128, [256] * 24, 2048, 2048, head, seed=2)
+        _check(lay, _q(2, 1, 32, 1, 128), lay.total_tokens - 1)
+
+
+def test_decode_132k_bf16_full_size():
+    # 4096-token ring + 127 blocks of 1000 + a 1024-token tail block.
+    lay = make_layout("bfloat16", 1, 8, 128, [1000] * 127 + [1024], 4096, 4096, 1234, seed=3, gap=0)
+    _check(lay, _q(3, 1, 32, 1, 128), lay.total_tokens - 1)
+
+
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
+def test_ragged_blocks_and_wrapped_ring(dtype):
+    lens = [1, 3, 1000, 7, 64, 65, 127, 129, 8, 9, 63]
+    lay = make_layout(dtype, 1, 4, 128, lens, 100, 90, 60, seed=5)
+    _check(lay, _q(5, 1, 16, 1, 128), lay.total_tokens - 1)
+
+
+def test_hot_only_single_segment():
+    lay = make_layout("bfloat16", 1, 8, 128, [], 512, 300, 0, seed=6)
+    _check(lay, _q(6, 1, 32, 1, 128), lay.total_tokens - 1)
+
+
+def test_archived_only_no_hot():
+    lay = make_layout("float16", 1, 8, 128, [300, 200], 64, 0, 0, seed=7)
+    _check(lay, _q(7, 1, 32, 1, 128), lay.total_tokens - 1)
+
+
+def test_causal_two_query_rows_fast_path():
+    # q_len 2 x groups 2 = 4 slots -> tensor-core kernel; rows see different key sets.
+    lay = make_layout("bfloat16", 1, 4, 128, [100, 50], 64, 40, 10, seed=8)
+    T = lay.total_tokens
+    _check(lay, _q(8, 1, 8, 2, 128), T - 2)
+    _check(lay, _q(9, 1, 8, 2, 128), T - 30)  # part of the hot window is in the future
+
+
+@pytest.mark.parametrize("B,H,Hkv,Lq,D,dtype", [
+    (1, 64, 8, 1, 128, "float16"),    # 8 slots per KV head -> CUDA-core kernel
+    (1, 2, 2, 4, 64, "float32"),      # tiny-model shape, float32 cache
+    (2, 8, 4, 1, 128, "bfloat16"),    # batch 2, tensor-core kernel
+    (1, 8, 2, 16, 64, "float16"),     # prefill-like chunk, causal
+    (1, 4, 4, 3, 256, "bfloat16"),    # head_dim 256
+    (1, 2, 1, 1, 16, "float32"),      # reference test-helper head_dim
+])
+def test_shapes(B, H, Hkv, Lq, D, dtype):
+    lay = make_layout(dtype, B, Hkv, D, [37, 64, 5, 200], 48, 45, 20, seed=11)
+    _check(lay, _q(11, B, H, Lq, D), lay.total_tokens - Lq)
+
+
+def test_split_count_invariance_and_determinism():
+    lay = make_layout("bfloat16", 1, 8, 128, [256] * 10 + [77], 256, 200, 100, seed=12)
+    q = _q(12, 1, 32, 1, 128)
+    pos = lay.total_tokens - 1
+    outs = [run_paged(lay, q, pos, max_splits=s)[0] for s in (1, 3, 0)]
+    for o in outs[1:]:
+        np.testing.assert_allclose(o, outs[0], atol=2e-6)
+    again = run_paged(lay, q, pos)[0]
+    np.testing.assert_array_equal(again, outs[2])
+
+
+CASES = golden_attention_cases()
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c["name"] for c in CASES])
+def test_segment_list_path_matches_reference_golden(case):
+    import torch
+
+    from rfsn_b200.attention_exact import run_segmented_attention as dev_attn
+    from _util import to_device_storage
+
+    segs = [(to_device_storage(k, case["dtype"]), to_device_storage(v, case["dtype"]), s) for k, v, s in case["segs"]]
+    out = dev_attn(torch.from_numpy(case["q"]).cuda(), segs, case["q_start"]).cpu().numpy()
+    err = float(np.abs(out - case["out"]).max())
+    assert err <= ATOL, err
+    assert err <= 1e-5, err
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c["name"] for c in CASES])
+def test_paged_path_matches_reference_golden(case):
+    """The same golden inputs laid out in an arena + page table."""
+    from _util import PagedLayout, TILE
+
+    dtype = case["dtype"]
+    B, Hkv = case["q"].shape[0], case["Hkv"]
+    D = case["q"].shape[3]
+    segs = case["segs"]
+    lens = [k.shape[2] for k, _, _ in segs]
+    rows = 16 + sum(lens) + 4 * len(lens)
+    store_dtype = segs[0][0].dtype
+    k_store = np.zeros((B * Hkv, rows, D), store_dtype)
+    v_store = np.zeros_like(k_store)
+    recs = np.zeros((len(segs) + 1, 4), np.int32)
+    row, tile = 16, 0
+    for i, (k, v, s) in enumerate(segs):
+        n = k.shape[2]
+        k_store[:, row:row + n] = k.reshape(B * Hkv, n, D)
+        v_store[:, row:row + n] = v.reshape(B * Hkv, n, D)
+        recs[i] = (row, s, n, tile)
+        row += n + 3
+        tile += (n + TILE - 1) // TILE
+    recs[len(segs), 3] = tile
+    lay = PagedLayout(dtype, B, Hkv, D, rows, 16, 0, 0, sum(lens), k_store, v_store, recs, lens, [s for _, _, s in segs])
+    out, _ = run_paged(lay, case["q"], case["q_start"])
+    err = float(np.abs(out - case["out"]).max())
+    assert err <= ATOL, err
+    assert err <= GUARD, err
+
+
+def test_lse_merge_kernel_matches_oracle():
+    import torch
+
+    from rfsn_b200 import _native as native
+
+    rng = np.random.default_rng(13)
+    P, rows, D = 5, 32, 128
+    outs = rng.standard_normal((P, rows, D), dtype=np.float32)
+    lses = (rng.standard_normal((P, rows)) * 4).astype(np.float32)
+    lses[2, 3] = -np.inf
+    ref = merge_partials(list(outs), list(lses))
+    o = torch.from_numpy(outs).cuda()
+    l = torch.from_numpy(lses).cuda()
+    res = torch.empty((rows, D), device="cuda")
+    lo = torch.empty((rows,), device="cuda")
+    native.check(native.lib().rfsn_lse_merge(o.data_ptr(), l.data_ptr(), P, rows, D, res.data_ptr(), lo.data_ptr(),
+                                             native.stream_ptr()), "lse_merge")
+    np.testing.assert_allclose(res.cpu().numpy(), ref, atol=1e-5)
+    m = np.max(lses, axis=0)
+    np.testing.assert_allclose(lo.cpu().numpy(), m + np.log(np.exp(lses - m).sum(0)), atol=1e-5)
+
+
+def test_empty_context_is_rejected_like_reference():
+    lay = make_layout("bfloat16", 1, 8, 128, [], 64, 0, 0, seed=14)
+    with pytest.raises(ValueError, match="at least one KV segment"):
+        run_paged(lay, _q(14, 1, 32, 1, 128), 0)

@@ -1,0 +1,68 @@
+"""Pins the oracle to the reference: the golden fixtures were produced by the
+reference's own modules (tests/golden/make_golden.py)."""
+
+import numpy as np
+import pytest
+
+from _util import golden_attention_cases, load_json
+from oracle.kv_ring import RingOracle
+from oracle.numerics import bf16_bits_to_f32, f32_to_bf16_bits, from_storage
+from oracle.segmented_attention import merge_partials, run_segmented_attention
+
+CASES = golden_attention_cases()
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c["name"] for c in CASES])
+@pytest.mark.parametrize("grouped", [False, True])
+def test_oracle_attention_matches_reference(case, grouped):
+    segs = [(from_storage(k, case["dtype"]), from_storage(v, case["dtype"]), s) for k, v, s in case["segs"]]
+    out = run_segmented_attention(case["q"], segs, case["q_start"], grouped=grouped)
+    np.testing.assert_allclose(out, case["out"], atol=2e-6, rtol=0)
+
+
+def test_oracle_empty_segments_raise_like_reference():
+    with pytest.raises(RuntimeError, match="at least one KV segment"):
+        run_segmented_attention(np.zeros((1, 1, 1, 4), np.float32), [], 0)
+
+
+def test_oracle_lse_merge_equals_unsplit():
+    case = CASES[1]
+    segs = [(from_storage(k, case["dtype"]), from_storage(v, case["dtype"]), s) for k, v, s in case["segs"]]
+    full, _ = run_segmented_attention(case["q"], segs, case["q_start"], return_lse=True)
+    parts = [run_segmented_attention(case["q"], segs[i:i + 2], case["q_start"], return_lse=True) for i in (0, 2, 4)]
+    merged = merge_partials([p[0] for p in parts], [p[1] for p in parts])
+    np.testing.assert_allclose(merged, full, atol=2e-6)
+
+
+RING = load_json("ring_traces.json")
+
+
+@pytest.mark.parametrize("name", sorted(RING))
+def test_ring_oracle_matches_reference_trace(name):
+    sc = RING[name]
+    ring = RingOracle(sc["hot_capacity"], sc["block_size"], exact_mode=sc["mode"] == "exact")
+    for step in sc["steps"]:
+        n = step["incoming"]
+        if "error" in step:
+            with pytest.raises(RuntimeError) as err:
+                ring.evict_for_append(n)
+                ring.append(n)
+            assert str(err.value) == step["error"]
+            continue
+        ring.evict_for_append(n)
+        ring.append(n)
+        assert (ring.head, ring.length, ring.start) == (step["hot_head_index"], step["hot_seq_len"], step["hot_start"])
+        assert ring.write_index == step["hot_write_index"]
+        assert ring.end == step["hot_end"]
+        assert [list(s) for s in ring.sealed] == [[b["start"], b["end"]] for b in step["blocks"]]
+        hot = [[s, n_] for _, n_, s in ring.hot_spans()]
+        assert [[b["start"], b["end"] - b["start"]] for b in step["blocks"]] + hot == step["segments"]
+
+
+def test_bf16_rounding_is_round_to_nearest_even():
+    x = np.array([1.0, 1.00390625, 1.01171875, -3.0e-3, 65504.0, 1e-30], np.float32)
+    y = bf16_bits_to_f32(f32_to_bf16_bits(x))
+    import torch
+
+    ref = torch.from_numpy(x).to(torch.bfloat16).to(torch.float32).numpy()
+    np.testing.assert_array_equal(y, ref)
