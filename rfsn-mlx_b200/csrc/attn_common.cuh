@@ -25,59 +25,76 @@ struct TileRef {
 struct PagedCursor {
     const int4* records;  // {row, pos, len, tile_begin}, n_blocks + 1 entries
     int n_blocks, archived_tiles;
-    // hot pieces
-    int h_row[2], h_pos[2], h_len[2];
+    // the two hot pieces
+    int h0_row, h0_pos, h0_len, h1_row, h1_pos, h1_len;
     // current position
     int span, tile_in_span, span_tiles, s_row, s_pos, s_len;
+    int4 next_rec;  // record span + 1, prefetched
 
     __device__ void init_hot(int ring_row0, int capacity, int head, int length, int start_pos) {
-        int first = min(length, capacity - head);
-        h_row[0] = ring_row0 + head;
-        h_pos[0] = start_pos;
-        h_len[0] = first;
-        h_row[1] = ring_row0;
-        h_pos[1] = start_pos + first;
-        h_len[1] = length - first;
+        const int first = min(length, capacity - head);
+        h0_row = ring_row0 + head;
+        h0_pos = start_pos;
+        h0_len = first;
+        h1_row = ring_row0;
+        h1_pos = start_pos + first;
+        h1_len = length - first;
     }
 
-    __device__ void load_span(int s) {
+    __device__ void set_span(int s, int4 rec) {
         span = s;
         if (s < n_blocks) {
-            int4 r = records[s];
-            s_row = r.x;
-            s_pos = r.y;
-            s_len = r.z;
+            s_row = rec.x;
+            s_pos = rec.y;
+            s_len = rec.z;
+            next_rec = (s + 1 < n_blocks) ? records[s + 1] : make_int4(0, 0, 0, 0);
+        } else if (s == n_blocks) {
+            s_row = h0_row;
+            s_pos = h0_pos;
+            s_len = h0_len;
+        } else if (s == n_blocks + 1) {
+            s_row = h1_row;
+            s_pos = h1_pos;
+            s_len = h1_len;
         } else {
-            int h = s - n_blocks;
-            if (h < 2) {
-                s_row = h_row[h];
-                s_pos = h_pos[h];
-                s_len = h_len[h];
-            } else {
-                s_row = s_pos = s_len = 0;
-            }
+            s_row = s_pos = s_len = 0;
         }
         span_tiles = (s_len + kTile - 1) / kTile;
     }
 
-    // Position the cursor on global tile index gt.
-    __device__ void seek(int gt) {
+    // Largest i in [0, n_blocks) with records[i].tile_begin <= gt, found by the
+    // 32 lanes of the calling warp together (two rounds of loads for up to
+    // ~1000 blocks instead of a dependent binary search). All lanes return it.
+    __device__ int warp_find(int gt) const {
+        const int lane = threadIdx.x & 31;
+        int lo = 0, hi = n_blocks;  // answer in [lo, hi)
+        while (hi - lo > 1) {
+            const int step = (hi - lo + 31) / 32;
+            const int idx = lo + lane * step;
+            const bool ok = idx < hi && records[idx].w <= gt;
+            const unsigned m = __ballot_sync(0xffffffffu, ok);
+            const int last = 31 - __clz(m);  // lane 0 always qualifies (records[lo].w <= gt)
+            lo = lo + last * step;
+            hi = min(hi, lo + step);
+        }
+        return lo;
+    }
+
+    // Position on global tile index gt. Called by a whole warp.
+    __device__ void seek_warp(int gt) {
         if (gt < archived_tiles) {
-            int lo = 0, hi = n_blocks - 1;  // largest i with tile_begin[i] <= gt
-            while (lo < hi) {
-                int mid = (lo + hi + 1) >> 1;
-                if (records[mid].w <= gt) lo = mid; else hi = mid - 1;
-            }
-            load_span(lo);
-            tile_in_span = gt - records[lo].w;
+            const int i = warp_find(gt);
+            const int4 rec = records[i];
+            set_span(i, rec);
+            tile_in_span = gt - rec.w;
         } else {
-            int rem = gt - archived_tiles;
-            int t0 = (h_len[0] + kTile - 1) / kTile;
+            const int rem = gt - archived_tiles;
+            const int t0 = (h0_len + kTile - 1) / kTile;
             if (rem < t0) {
-                load_span(n_blocks);
+                set_span(n_blocks, make_int4(0, 0, 0, 0));
                 tile_in_span = rem;
             } else {
-                load_span(n_blocks + 1);
+                set_span(n_blocks + 1, make_int4(0, 0, 0, 0));
                 tile_in_span = rem - t0;
             }
         }
@@ -86,7 +103,7 @@ struct PagedCursor {
 
     __device__ void skip_empty() {
         while (span_tiles == 0 && span < n_blocks + 2) {
-            load_span(span + 1);
+            set_span(span + 1, next_rec);
             tile_in_span = 0;
         }
     }
@@ -103,7 +120,7 @@ struct PagedCursor {
 
     __device__ void advance() {
         if (++tile_in_span >= span_tiles) {
-            load_span(span + 1);
+            set_span(span + 1, next_rec);
             tile_in_span = 0;
             skip_empty();
         }
@@ -117,14 +134,21 @@ struct PagedCursor {
 //   out = O / max(L, 1e-9)           (attention_exact.py:155-164),
 //   lse = (M + log2 L) * ln 2        (natural log, for cross-GPU merges).
 // Scores are kept in log2 units (q pre-multiplied by log2 e).
-// Must be called by all `nthreads` participating threads (thread 0 included)
-// after the CTA partial has been written. `flag` is a shared int and `sbuf`
-// shared scratch of at least nslots * (splits + 2) floats.
+//
+// The merge is latency-critical (it runs after every other CTA of the group
+// has finished), so all loads are issued in parallel: the per-split (m, l)
+// pairs in one sweep, the per-slot max / weight / sum by one warp per slot
+// with shuffles, and the outputs as float4 loads eight splits deep per thread.
+// Must be called by all `nthreads` (a multiple of 32) participating threads
+// (thread 0 included) after the CTA partial has been written. `flag` is a
+// shared int; `sbuf` is shared scratch of merge_scratch_floats() floats.
+__host__ __device__ constexpr int merge_scratch_floats(int nslots, int splits) { return 2 * nslots * splits + 2 * nslots; }
+
 __device__ __forceinline__ void finish_splits(const WsView& ws, int counter_idx, int part_base, int split_stride,
                                               int splits, int slot0, int nslots, int head_dim, const OutMap& om,
                                               int bh, float* out, float* lse, int* flag, float* sbuf, int bar_id,
                                               int nthreads) {
-    const int tid = threadIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = nthreads >> 5;
     __threadfence();
     named_barrier_sync(bar_id, nthreads);
     if (splits > 1) {
@@ -136,38 +160,83 @@ __device__ __forceinline__ void finish_splits(const WsView& ws, int counter_idx,
         if (!*flag) return;
         __threadfence();
     }
-    float* wts = sbuf;                      // [nslots][splits] weights 2^(m_s - M)
-    float* totals = sbuf + nslots * splits; // [nslots] L
+    float* wts = sbuf;                          // [nslots][splits] m_s, then weights
+    float* ls = sbuf + nslots * splits;         // [nslots][splits] l_s
+    float* totals = ls + nslots * splits;       // [nslots] L
     for (int i = tid; i < nslots * splits; i += nthreads) {
         const int sl = i / splits, s = i - sl * splits;
-        wts[i] = __ldcg(ws.m + part_base + s * split_stride + slot0 + sl);
+        const int p = part_base + s * split_stride + slot0 + sl;
+        wts[i] = __ldcg(ws.m + p);
+        ls[i] = __ldcg(ws.l + p);
     }
     named_barrier_sync(bar_id, nthreads);
-    if (tid < nslots) {
-        float* w = wts + tid * splits;
+    for (int sl = warp; sl < nslots; sl += nwarps) {
+        float* w = wts + sl * splits;
+        const float* l = ls + sl * splits;
         float M = -CUDART_INF_F;
-        for (int s = 0; s < splits; ++s) M = fmaxf(M, w[s]);
+        for (int s = lane; s < splits; s += 32) M = fmaxf(M, w[s]);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
         float L = 0.f;
-        for (int s = 0; s < splits; ++s) {
+        for (int s = lane; s < splits; s += 32) {
             const float ws_ = (M == -CUDART_INF_F) ? 0.f : exp2f(w[s] - M);
             w[s] = ws_;
-            L += ws_ * __ldcg(ws.l + part_base + s * split_stride + slot0 + tid);
+            L += ws_ * l[s];
         }
-        totals[tid] = L;
-        if (lse != nullptr) {
-            lse[om.row(bh, slot0 + tid)] = (L > 0.f) ? (M + log2f(L)) * 0.69314718055994531f : -CUDART_INF_F;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+        if (lane == 0) {
+            totals[sl] = L;
+            if (lse != nullptr) lse[om.row(bh, slot0 + sl)] = (L > 0.f) ? (M + log2f(L)) * 0.69314718055994531f : -CUDART_INF_F;
         }
     }
     named_barrier_sync(bar_id, nthreads);
-    for (int idx = tid; idx < nslots * head_dim; idx += nthreads) {
-        const int sl = idx / head_dim, d = idx - sl * head_dim;
-        const float* w = wts + sl * splits;
-        float O = 0.f;
-        for (int s = 0; s < splits; ++s) {
-            const size_t p = (size_t)(part_base + s * split_stride + slot0 + sl);
-            O += w[s] * __ldcg(ws.o + p * head_dim + d);
+    if ((head_dim & 3) == 0) {
+        const int d4n = head_dim >> 2;
+        for (int idx = tid; idx < nslots * d4n; idx += nthreads) {
+            const int sl = idx / d4n, d4 = idx - sl * d4n;
+            const float* w = wts + sl * splits;
+            const float4* base = reinterpret_cast<const float4*>(ws.o) +
+                                 (size_t)(part_base + slot0 + sl) * d4n + d4;
+            const size_t stride = (size_t)split_stride * d4n;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            int s = 0;
+            for (; s + 8 <= splits; s += 8) {
+                float4 v[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) v[u] = __ldcg(base + (size_t)(s + u) * stride);
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const float c = w[s + u];
+                    acc.x += c * v[u].x;
+                    acc.y += c * v[u].y;
+                    acc.z += c * v[u].z;
+                    acc.w += c * v[u].w;
+                }
+            }
+            for (; s < splits; ++s) {
+                const float4 v = __ldcg(base + (size_t)s * stride);
+                const float c = w[s];
+                acc.x += c * v.x;
+                acc.y += c * v.y;
+                acc.z += c * v.z;
+                acc.w += c * v.w;
+            }
+            const float inv = 1.f / fmaxf(totals[sl], 1e-9f);
+            float4 r = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+            *reinterpret_cast<float4*>(out + om.row(bh, slot0 + sl) * head_dim + 4 * d4) = r;
         }
-        out[om.row(bh, slot0 + sl) * head_dim + d] = O / fmaxf(totals[sl], 1e-9f);
+    } else {
+        for (int idx = tid; idx < nslots * head_dim; idx += nthreads) {
+            const int sl = idx / head_dim, d = idx - sl * head_dim;
+            const float* w = wts + sl * splits;
+            float O = 0.f;
+            for (int s = 0; s < splits; ++s) {
+                const size_t p = (size_t)(part_base + s * split_stride + slot0 + sl);
+                O += w[s] * __ldcg(ws.o + p * head_dim + d);
+            }
+            out[om.row(bh, slot0 + sl) * head_dim + d] = O / fmaxf(totals[sl], 1e-9f);
+        }
     }
     if (splits > 1 && tid == 0) ws.counters[counter_idx] = 0;
 }

@@ -131,7 +131,7 @@ constexpr int kGenericMaxSplits = 256;
 int generic_max_splits(int head_dim) {
     // finish_splits scratch in the generic kernel lives in the staged-key buffer.
     const int avail = 32 * (head_dim + 1) + 32 * head_dim;
-    int m = avail / 8 - 2;
+    int m = avail / 16 - 1;
     return m < kGenericMaxSplits ? m : kGenericMaxSplits;
 }
 

@@ -35,8 +35,8 @@ constexpr int NCW = 4;                       // consumer warps (one 16-key strip
 constexpr int NTHREADS = (NCW + 1) * 32;     // + one producer warp
 constexpr int SLOTS = 4;                     // query slots per KV head handled
 constexpr int HALF_BYTES = kTile * 128;      // 64 rows x 64 elements x 2 B
-// The split merge keeps nslots * (splits + 2) weights in red_o (NCW * SLOTS * D floats).
-constexpr int MAX_SPLITS = 256;
+// The split merge keeps 2 * nslots * (splits + 1) floats in red_o (NCW * SLOTS * D floats).
+constexpr int MAX_SPLITS = 240;
 
 
 template <int STAGES>
@@ -78,15 +78,21 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
 
     if (warp == NCW) {
         // ---------------- producer: one elected lane issues all TMA loads ----------------
-        if (lane == 0 && ntiles > 0) {
-            prefetch_tmap(&mapK64);
-            prefetch_tmap(&mapV64);
-            PagedCursor cur;
+        PagedCursor cur;
+        if (ntiles > 0) {
+            if (lane == 0) {
+                prefetch_tmap(&mapK64);
+                prefetch_tmap(&mapV64);
+                prefetch_tmap(&mapK8);
+                prefetch_tmap(&mapV8);
+            }
             cur.records = p.records;
             cur.n_blocks = p.n_blocks;
             cur.archived_tiles = p.archived_tiles;
             cur.init_hot(p.ring_row0, p.capacity, p.head, p.hlen, p.hstart);
-            cur.seek(tile0);
+            cur.seek_warp(tile0);
+        }
+        if (lane == 0 && ntiles > 0) {
             const int row_base = bh * p.rows;
             for (int it = 0; it < ntiles; ++it) {
                 const int s = it % STAGES;

@@ -103,7 +103,7 @@ __global__ void __launch_bounds__(NT) generic_attn_kernel(const Params p) {
             pc.n_blocks = p.n_blocks;
             pc.archived_tiles = p.archived_tiles;
             pc.init_hot(p.ring_row0, p.capacity, p.head, p.hlen, p.hstart);
-            pc.seek(tile0);
+            pc.seek_warp(tile0);
         } else {
             sc.segs = p.segs;
             sc.n = p.n_segs;
