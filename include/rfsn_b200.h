@@ -248,6 +248,32 @@ RFSN_API rfsn_status rfsn_lse_merge(const float* parts_out, const float* parts_l
                            int n_parts, int rows, int head_dim,
                            float* out, float* lse_out, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Paged attention without any device allocation. No counterpart in the
+ * reference (which has no native interface); this is a variant of
+ * rfsn_paged_attention for callers that cannot allocate device memory when
+ * they run attention (engines that own all device memory through their own
+ * pool, frozen memory budgets, plugin hosts that only pass inputs and
+ * outputs). Same arguments and results as rfsn_paged_attention, minus the
+ * workspace: the split scratch lives in one built-in device array of
+ * RFSN_NOALLOC_SCRATCH_BYTES that every GPU loading the library keeps until
+ * the process exits. Calls sharing a device share the array; calls that
+ * overlap on the GPU race and must be ordered by the caller. Shapes whose
+ * split scratch does not fit are rejected with RFSN_ERR_OVERFLOW (lower
+ * max_splits, or use rfsn_paged_attention). The first call on each device
+ * looks up the array's device address (cudaGetSymbolAddress) and should be
+ * made before any stream capture.
+ * ---------------------------------------------------------------------- */
+#define RFSN_NOALLOC_SCRATCH_BYTES (8u << 20)
+
+RFSN_API rfsn_status rfsn_paged_attention_noalloc(const rfsn_arena* arena,
+                                         const float* q, int batch, int q_heads, int kv_heads,
+                                         int q_len, int q_pos0,
+                                         const rfsn_page_table* table,
+                                         const rfsn_hot_window* hot,
+                                         float* out, float* lse,
+                                         int max_splits, void* stream);
+
 /* Number of kernels this library has launched in the process so far
  * (instrumentation: lets callers count native launches in a timed region). */
 RFSN_API uint64_t rfsn_launch_count(void);

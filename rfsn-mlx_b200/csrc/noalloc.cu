@@ -1,0 +1,84 @@
+// rfsn_paged_attention_noalloc: paged attention that allocates nothing.
+//
+// Some callers cannot call cudaMalloc at the point where they run attention:
+// an inference engine that owns every byte of device memory through its own
+// pool (and forbids allocations behind its back), code running while a
+// memory budget is frozen, or a plugin host that only hands out the input and
+// output buffers. For them this entry point keeps the split-KV scratch (arrival
+// counters, per-split partial results) in one fixed array compiled into the
+// library, so the call needs no workspace argument and performs no device
+// allocation of any kind.
+//
+// The array is kNoallocScratchBytes long and every GPU that loads this library
+// holds its own copy until the process exits. All calls on a device share it
+// and it keeps whatever the previous call left there; the counters that must
+// start at zero are cleared (cudaMemsetAsync, no allocation) at the start of
+// every call. Calls whose execution overlaps on the GPU (different streams, or
+// different host threads) race on the array and must be ordered by the caller.
+//
+// The device address of the array is looked up with cudaGetSymbolAddress the
+// first time the entry point runs on each device, with that device current.
+// That first call on a device therefore performs set-up work and should be
+// made before any CUDA stream capture begins.
+#include <mutex>
+#include <string>
+
+#include "common.cuh"
+
+namespace {
+
+constexpr size_t kNoallocScratchBytes = RFSN_NOALLOC_SCRATCH_BYTES;
+
+// File-scope device scratch (zero at module load). In host code this name is
+// only a stand-in for the symbol; its device address comes from
+// cudaGetSymbolAddress below and is the only pointer passed to kernels.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_setup_mutex;
+void* g_scratch_addr[kMaxDevices] = {nullptr};
+
+rfsn_status scratch_address(void** out) {
+    int dev = 0;
+    RFSN_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) {
+        rfsn::set_error("rfsn_paged_attention_noalloc: device index %d above %d", dev, kMaxDevices - 1);
+        return RFSN_ERR_UNSUPPORTED;
+    }
+    std::lock_guard<std::mutex> lock(g_setup_mutex);
+    if (g_scratch_addr[dev] == nullptr) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || p == nullptr) {
+            return rfsn::cuda_status(e != cudaSuccess ? e : cudaErrorInvalidSymbol, "cudaGetSymbolAddress(g_noalloc_scratch)");
+        }
+        g_scratch_addr[dev] = p;
+    }
+    *out = g_scratch_addr[dev];
+    return RFSN_OK;
+}
+
+}  // namespace
+
+extern "C" rfsn_status rfsn_paged_attention_noalloc(const rfsn_arena* arena, const float* q, int batch, int q_heads,
+                                                    int kv_heads, int q_len, int q_pos0, const rfsn_page_table* table,
+                                                    const rfsn_hot_window* hot, float* out, float* lse, int max_splits,
+                                                    void* stream) {
+    void* scratch = nullptr;
+    rfsn_status st = scratch_address(&scratch);
+    if (st != RFSN_OK) return st;
+    // Error word and arrival counters must start at zero.
+    RFSN_CUDA(cudaMemsetAsync(scratch, 0, 256 + sizeof(int) * (size_t)rfsn::kMaxCounters,
+                              static_cast<cudaStream_t>(stream)));
+    st = rfsn_paged_attention(arena, q, batch, q_heads, kv_heads, q_len, q_pos0, table, hot, out, lse, scratch,
+                              kNoallocScratchBytes, max_splits, stream);
+    if (st == RFSN_ERR_OVERFLOW) {
+        // The shape needs more split scratch than the built-in array holds.
+        const std::string inner = rfsn_last_error();
+        rfsn::set_error(
+            "rfsn_paged_attention_noalloc: the built-in scratch holds %zu bytes and this call needs more (%s); pass "
+            "a smaller max_splits or use rfsn_paged_attention with a caller-provided workspace",
+            kNoallocScratchBytes, inner.c_str());
+    }
+    return st;
+}

@@ -56,6 +56,7 @@ EXPORTED_SYMBOLS = (
     "rfsn_lse_merge",
     "rfsn_workspace_check",
     "rfsn_launch_count",
+    "rfsn_paged_attention_noalloc",
 )
 
 
@@ -143,6 +144,10 @@ def load_library() -> ctypes.CDLL:
         "rfsn_lse_merge": (i32, [vp, vp, i32, i32, i32, vp, vp, vp]),
         "rfsn_workspace_check": (i32, [vp, vp, i64]),
         "rfsn_launch_count": (ctypes.c_uint64, []),
+        "rfsn_paged_attention_noalloc": (
+            i32,
+            [vp, vp, i32, i32, i32, i32, i32, ctypes.POINTER(PageTableC), ctypes.POINTER(HotWindowC), vp, vp, i32, vp],
+        ),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
