@@ -1,0 +1,194 @@
+"""Host-side logic of the drop-in cache on CPU (no GPU): ring / seal / page
+table / residency replayed against the reference's traces, plus the block
+manager, storage and config contracts."""
+
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from cache_replay import replay_residency, replay_ring, residency_names, ring_names
+from fake_ops import FakeDeviceOps
+from rfsn_b200 import (
+    BlockId,
+    BlockLocation,
+    BlockManager,
+    BlockManifest,
+    BlockSpan,
+    BlockStorage,
+    PageTable,
+    RFSNConfig,
+    ResidencyManager,
+)
+from rfsn_b200.cache import _RowAllocator
+
+
+@pytest.mark.parametrize("name", ring_names())
+def test_ring_and_page_table_match_reference_trace(name):
+    replay_ring(name, FakeDeviceOps)
+
+
+@pytest.mark.parametrize("name", residency_names())
+def test_residency_matches_reference_trace(name):
+    replay_residency(name, FakeDeviceOps)
+
+
+def test_device_page_table_records():
+    cache = replay_ring("odd_hot10_bs3", FakeDeviceOps)
+    segs = cache.get_attention_segments()
+    table, n, toks, tiles = segs.table
+    recs = table[: n + 1].numpy()
+    blocks = cache.block_manager.iter_blocks(layer_id=0)
+    assert n == len(blocks)
+    tile = 0
+    for rec, m in zip(recs[:n], blocks):
+        assert (rec[1], rec[2], rec[3]) == (m.logical_start, m.token_count, tile)
+        assert rec[0] == cache._resident_rows[m.block_id]
+        tile += (m.token_count + 63) // 64
+    assert recs[n][3] == tiles == tile
+    assert toks == sum(m.token_count for m in blocks)
+
+
+# --------------------------------------------------------------------------------- block manager
+def _manifest(name, start, end, where, layer=0, materializable=True):
+    return BlockManifest(
+        block_id=BlockId("m", layer, name), span=BlockSpan(start, end), codec_version="v11-exact-kv",
+        dtype="float32", shape_metadata={"keys": (1, 1, end - start, 2), "values": (1, 1, end - start, 2)},
+        checksum=f"c-{name}", residency=where, materializable=materializable,
+    )
+
+
+def test_page_table_sorts_locates_and_counts():
+    bm = BlockManager("m")
+    for m in (
+        _manifest("c", 8, 12, BlockLocation.COLD_DISK),
+        _manifest("a", 0, 4, BlockLocation.HOT),
+        _manifest("d", 12, 16, BlockLocation.MISSING, materializable=False),
+        _manifest("b", 4, 8, BlockLocation.WARM_RAM),
+    ):
+        bm.register_block(m)
+    assert [m.block_id.block_id for m in bm.locate_blocks_for_range(0, 2, 14)] == ["a", "b", "c", "d"]
+    bm.mark_unmaterializable(layer_id=0, span=BlockSpan(8, 12), reason="bad")
+    stats = bm.get_residency_stats()
+    assert stats["total_blocks"] == 4 and stats["total_tokens"] == 16
+    assert stats["by_location"]["warm_ram"]["blocks"] == 1
+    assert stats["unmaterializable_blocks"] == 2
+    with pytest.raises(ValueError, match="overlaps"):
+        bm.register_block(_manifest("e", 3, 6, BlockLocation.COLD_DISK))
+    with pytest.raises(ValueError, match="already registered"):
+        bm.register_block(_manifest("a", 40, 44, BlockLocation.HOT))
+    with pytest.raises(KeyError, match="Unknown block_id"):
+        bm.get_block(BlockId("m", 0, "zz"))
+    with pytest.raises(ValueError, match="mark_missing"):
+        bm.promote_block(BlockId("m", 0, "a"), BlockLocation.MISSING)
+
+
+def test_metadata_json_round_trip():
+    bm = BlockManager("m")
+    bm.register_block(_manifest("x", 0, 4, BlockLocation.WARM_RAM))
+    bm.register_block(_manifest("y", 0, 8, BlockLocation.COLD_DISK, layer=1))
+    blob = json.loads(json.dumps(bm.serialize_metadata()))
+    back = BlockManager.deserialize_metadata(blob)
+    assert [m.to_dict() for m in back.iter_blocks()] == [m.to_dict() for m in bm.iter_blocks()]
+    table = PageTable.from_dict(blob["page_table"])
+    assert table.locate(1, 0, 8)[0].checksum == "c-y"
+    keys = set(bm.iter_blocks()[0].to_dict())
+    assert {"model_id", "layer_id", "block_id", "logical_start", "logical_end", "token_count", "codec_version",
+            "dtype", "shape_metadata", "checksum", "residency", "created_at", "last_accessed_at", "pin_count",
+            "ref_count", "payload_format", "payload_path", "manifest_path", "materializable",
+            "failure_reason"} == keys
+
+
+def test_lru_victim_uses_access_time_then_position():
+    rm = ResidencyManager()
+    ms = [_manifest(n, s, s + 4, BlockLocation.WARM_RAM) for n, s in (("a", 0), ("b", 4), ("c", 8))]
+    for m, t in zip(ms, (5.0, 1.0, 1.0)):
+        m.touch(timestamp=t)
+    assert rm.choose_warm_eviction_victim(ms).block_id.block_id == "b"
+    assert rm.choose_warm_eviction_victim(ms, protected_block_id=ms[1].block_id).block_id.block_id == "c"
+    ms[2].pin_count = 1
+    assert rm.choose_warm_eviction_victim(ms, protected_block_id=ms[1].block_id).block_id.block_id == "a"
+
+
+# --------------------------------------------------------------------------------- storage
+def _payload(n):
+    keys = np.arange(n * 2, dtype=np.float32).reshape(1, 1, n, 2)
+    return {"keys": keys, "values": keys + 100}
+
+
+def test_storage_round_trip_and_rescan(tmp_path):
+    st = BlockStorage(tmp_path)
+    m = _manifest("blk", 0, 4, BlockLocation.WARM_RAM)
+    st.persist_block(m, _payload(4))
+    assert m.residency == BlockLocation.COLD_DISK and len(m.checksum) == 64
+    assert Path(m.payload_path).name == "m.layer0.blk.npz"
+    bm = BlockManager("m")
+    scanned = st.rebuild_manager(bm)
+    assert [x.checksum for x in scanned] == [m.checksum]
+    loaded = st.load_block(scanned[0])
+    np.testing.assert_array_equal(loaded["values"], _payload(4)["values"])
+
+
+@pytest.mark.parametrize("damage,reason", [
+    ("delete", "missing"),
+    ("tamper", "checksum mismatch"),
+])
+def test_storage_failures_mark_missing_without_raising(tmp_path, damage, reason):
+    st = BlockStorage(tmp_path)
+    m = _manifest("blk", 0, 4, BlockLocation.WARM_RAM)
+    st.persist_block(m, _payload(4))
+    p = Path(m.payload_path)
+    if damage == "delete":
+        p.unlink()
+    else:
+        p.write_bytes(b"not an npz")
+    assert st.load_block(m) is None
+    assert m.residency == BlockLocation.MISSING and not m.materializable
+    assert reason in m.failure_reason
+    if damage == "tamper":
+        assert any(st.quarantine_dir.iterdir())
+
+
+def test_storage_rejects_bad_payloads(tmp_path):
+    st = BlockStorage(tmp_path)
+    m = _manifest("blk", 0, 4, BlockLocation.WARM_RAM)
+    with pytest.raises(ValueError, match="same dtype"):
+        st.persist_block(m, {"keys": np.zeros((1, 1, 4, 2), np.float32), "values": np.zeros((1, 1, 4, 2), np.float16)})
+    with pytest.raises(ValueError, match="shape mismatch"):
+        st.persist_block(m, _payload(3))
+
+
+# --------------------------------------------------------------------------------- config
+@pytest.mark.parametrize("kwargs,message", [
+    (dict(hidden_dim=30), "must equal num_heads"),
+    (dict(num_kv_heads=3), "divisible"),
+    (dict(hot_capacity=4096), "hot_capacity <= warm_capacity"),
+    (dict(block_size_seq=0), "block_size_seq"),
+    (dict(model_dtype="int8"), "model_dtype"),
+    (dict(session_id="bad id!"), "session_id"),
+])
+def test_config_validation_matches_reference(kwargs, message):
+    base = dict(hidden_dim=32, num_heads=2, head_dim=16)
+    base.update(kwargs)
+    with pytest.raises(ValueError, match=message):
+        RFSNConfig(**base)
+
+
+def test_config_defaults():
+    cfg = RFSNConfig()
+    assert cfg.num_kv_heads == cfg.num_heads and cfg.ffn_dim == 4 * cfg.hidden_dim and cfg.kv_groups == 1
+
+
+def test_row_allocator_first_fit_and_coalescing():
+    a = _RowAllocator(10, 30)
+    r1, r2, r3 = a.allocate(5), a.allocate(5), a.allocate(5)
+    assert (r1, r2, r3) == (10, 15, 20)
+    a.release(15, 5)
+    a.release(10, 5)
+    assert a.free[0] == [10, 20]
+    assert a.allocate(12) is None
+    a.release(20, 5)
+    assert a.free == [[10, 30]]
+    a.grow(40)
+    assert a.allocate(30) == 10
