@@ -30,29 +30,47 @@ def shard_range(n_blocks: int, rank: int, world: int) -> tuple[int, int]:
     return n_blocks * rank // world, n_blocks * (rank + 1) // world
 
 
-def merge_across_ranks(out: torch.Tensor, lse: torch.Tensor, group: Optional[dist.ProcessGroup] = None) -> torch.Tensor:
-    """All-gather per-rank (out [B,H,Lq,D], lse [B,H,Lq]) and LSE-merge them.
+def gather_parts(out: torch.Tensor, lse: torch.Tensor, group: Optional[dist.ProcessGroup] = None):
+    """All-gather every rank's (out [B,H,Lq,D], lse [B,H,Lq]) in rank order.
 
-    Every rank returns the merged result. With one rank this is the identity.
+    Returns (parts_out [P, rows, D], parts_lse [P, rows]) with rows = B*H*Lq.
+    One collective of P x rows x (D + 1) float32 values: the output and LSE
+    of a rank travel packed in one buffer.
     """
-    world = dist.get_world_size(group) if dist.is_initialized() else 1
-    if world == 1:
-        return out
+    world = dist.get_world_size(group)
     B, H, Lq, D = out.shape
     rows = B * H * Lq
-    packed = torch.cat([out.reshape(-1), lse.reshape(-1)])
-    gathered = torch.empty((world, packed.numel()), dtype=packed.dtype, device=packed.device)
-    dist.all_gather_into_tensor(gathered, packed, group=group)
-    parts_out = gathered[:, : rows * D].contiguous()
-    parts_lse = gathered[:, rows * D:].contiguous()
-    merged = torch.empty_like(out)
+    packed = torch.cat([out.reshape(-1).float(), lse.reshape(-1).float()])
+    if dist.get_backend(group) == "nccl":
+        gathered = torch.empty((world, packed.numel()), dtype=packed.dtype, device=packed.device)
+        dist.all_gather_into_tensor(gathered, packed, group=group)
+    else:
+        chunks = [torch.empty_like(packed) for _ in range(world)]
+        dist.all_gather(chunks, packed, group=group)
+        gathered = torch.stack(chunks)
+    return gathered[:, : rows * D].reshape(world, rows, D), gathered[:, rows * D:].reshape(world, rows)
+
+
+def merge_parts(parts_out: torch.Tensor, parts_lse: torch.Tensor, shape) -> torch.Tensor:
+    """LSE-merge gathered parts on the device (rfsn_lse_merge, rank order)."""
+    world, rows, D = parts_out.shape
+    po, pl = parts_out.contiguous(), parts_lse.contiguous()
+    merged = torch.empty(shape, dtype=torch.float32, device=po.device)
     native.check(
-        native.lib().rfsn_lse_merge(
-            parts_out.data_ptr(), parts_lse.data_ptr(), world, rows, D, merged.data_ptr(), None, native.stream_ptr()
-        ),
+        native.lib().rfsn_lse_merge(po.data_ptr(), pl.data_ptr(), world, rows, D, merged.data_ptr(), None,
+                                    native.stream_ptr()),
         "rfsn_lse_merge",
     )
     return merged
+
+
+def merge_across_ranks(out: torch.Tensor, lse: torch.Tensor, group: Optional[dist.ProcessGroup] = None) -> torch.Tensor:
+    """All-gather per-rank (out, lse) and LSE-merge them; every rank returns
+    the merged result. With one rank (or no process group) this is the identity."""
+    if not dist.is_initialized() or dist.get_world_size(group) == 1:
+        return out
+    parts_out, parts_lse = gather_parts(out, lse, group)
+    return merge_parts(parts_out, parts_lse, out.shape)
 
 
 def sharded_decode_step(cache: LayerKVCache, q: torch.Tensor, k: Optional[torch.Tensor], v: Optional[torch.Tensor],
