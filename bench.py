@@ -207,7 +207,7 @@ def max_over_ranks(x: float, world: int) -> float:
 
 
 # ------------------------------------------------------------------------------------ measurements
-def device_throughput(cache, w, world, steps, warmup, calls_per_step, *, collective: bool):
+def device_throughput(cache, w, world, steps, warmup, calls_per_step, *, collective: bool, peers=None):
     """calls/s with inputs resident: CUDA-graph-captured calls, CUDA events."""
     import torch
 
@@ -222,6 +222,8 @@ def device_throughput(cache, w, world, steps, warmup, calls_per_step, *, collect
     use_coll = collective and world > 1
 
     def one_call():
+        if use_coll and peers is not None:
+            return paged_attention(cache, q, pos, segs, peers=peers)
         if use_coll:
             out, lse = paged_attention(cache, q, pos, segs, want_lse=True)
             return merge_across_ranks(out, lse)
@@ -256,7 +258,7 @@ def device_throughput(cache, w, world, steps, warmup, calls_per_step, *, collect
     return ms, launches_per_step * steps
 
 
-def e2e_throughput(cache, w, world, owns_hot, steps, calls_per_step):
+def e2e_throughput(cache, w, world, owns_hot, steps, calls_per_step, peers=None):
     """calls/s through the public API with pinned host inputs and a host read-back every call."""
     import torch
 
@@ -287,7 +289,8 @@ def e2e_throughput(cache, w, world, owns_hot, steps, calls_per_step):
         if world == 1:
             out = attention_step(q, k, v, cache, p)
         else:
-            out = sharded_decode_step(cache, q, k if owns_hot else None, v if owns_hot else None, p, owns_hot=owns_hot)
+            out = sharded_decode_step(cache, q, k if owns_hot else None, v if owns_hot else None, p, owns_hot=owns_hot,
+                                      peers=peers)
         out_h.copy_(out, non_blocking=True)
         torch.cuda.current_stream().synchronize()
 
@@ -381,12 +384,18 @@ def run_ours(args, w):
     cache, owns_hot, local_tokens, total_tokens = build_shard(w, rank, world, device, extra)
     torch.cuda.synchronize()
 
+    peers = None
+    if world > 1 and args.merge == "p2p":
+        from rfsn_b200.sharded import PeerGroup
+
+        peers = PeerGroup(w["kv_heads"], w["head_dim"])
     peak, peak_kind = measured_peaks()
     sampler = ClockSampler(device.index).start()
     # kernel-only (local attention, no collective): roofline of the decode kernel
     k_ms, _ = device_throughput(cache, w, world, args.steps, args.warmup, args.calls_per_step, collective=False)
     # full call (local attention + all-gather + merge when N > 1)
-    ms, launches = device_throughput(cache, w, world, args.steps, args.warmup, args.calls_per_step, collective=True)
+    ms, launches = device_throughput(cache, w, world, args.steps, args.warmup, args.calls_per_step, collective=True,
+                                     peers=peers)
     clocks = sampler.stop()
     ms = max_over_ranks(ms, world)
     k_ms_max = max_over_ranks(k_ms, world)
@@ -399,7 +408,7 @@ def run_ours(args, w):
     achieved = local_bytes / k_call_s / 1e9
 
     # e2e through the public API (appends the new token each call)
-    e_elapsed, e_n, e_launches, h2d, d2h = e2e_throughput(cache, w, world, owns_hot, args.steps, e2e_calls)
+    e_elapsed, e_n, e_launches, h2d, d2h = e2e_throughput(cache, w, world, owns_hot, args.steps, e2e_calls, peers)
     e_elapsed = max_over_ranks(e_elapsed, world)
 
     traffic = None
@@ -444,7 +453,9 @@ def run_ours(args, w):
                 "context_tokens": total_tokens,
                 "calls_per_step": args.calls_per_step,
                 "l2": f"inputs larger than L2: {algorithmic_bytes(w, total_tokens) / 1e6:.0f} MB of K/V per call",
-                "parallelism": f"context-sharded over {world} GPU(s) by archived block, LSE merge via NCCL all-gather"
+                "parallelism": (f"context-sharded over {world} GPUs by archived block; LSE merge "
+                                + ("fused into the attention kernel over NVLink (CUDA IPC mailboxes)"
+                                   if args.merge == "p2p" else "via NCCL all-gather + merge kernel"))
                 if world > 1 else "1 GPU",
             },
             "us_per_call": per_call_ms * 1e3,
@@ -547,6 +558,8 @@ def main() -> int:
     ap.add_argument("--calls-per-step", type=int, default=200)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--merge", choices=["p2p", "nccl"], default="p2p",
+                    help="cross-GPU merge for N > 1: fused NVLink mailboxes (default) or NCCL all-gather")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

@@ -278,6 +278,42 @@ RFSN_API rfsn_status rfsn_paged_attention_noalloc(const rfsn_arena* arena,
  * (instrumentation: lets callers count native launches in a timed region). */
 RFSN_API uint64_t rfsn_launch_count(void);
 
+/* ------------------------------------------------------------------------
+ * Sharded decode with the cross-GPU merge fused into the attention kernel.
+ *
+ * The reference has no multi-GPU path. For a context whose archived blocks
+ * are partitioned over the GPUs of one node (one process per GPU), each rank
+ * attends over its own blocks; the last CTA of every KV head then stores its
+ * (output, LSE) into every rank's mailbox over NVLink and merges the parts of
+ * all ranks in rank order (the merge of attention_exact.py:141-164), so every
+ * rank ends with the full result after one kernel, without a collective
+ * library call. Waits for peers are bounded (rfsn_peer_group_set_timeout,
+ * default 2 s) and report RFSN_ERR_DEVICE through rfsn_workspace_check.
+ *
+ * Set-up per rank: rfsn_peer_group_create (allocates the mailbox on the
+ * current device and writes its CUDA IPC handle, rfsn_peer_ipc_handle_bytes()
+ * bytes), exchange the handles (e.g. an all-gather), then
+ * rfsn_peer_group_connect with all handles in rank order. Every rank must make
+ * the same sequence of rfsn_paged_attention_peer calls.
+ * ---------------------------------------------------------------------- */
+typedef struct rfsn_peer_group rfsn_peer_group;
+
+RFSN_API int rfsn_peer_ipc_handle_bytes(void);
+RFSN_API rfsn_status rfsn_peer_group_create(int world, int rank, int groups, int head_dim,
+                                            rfsn_peer_group** out, void* ipc_handle_out);
+RFSN_API rfsn_status rfsn_peer_group_connect(rfsn_peer_group* group, const void* all_handles);
+RFSN_API rfsn_status rfsn_peer_group_set_timeout(rfsn_peer_group* group, int64_t timeout_us);
+RFSN_API rfsn_status rfsn_peer_group_destroy(rfsn_peer_group* group);
+RFSN_API rfsn_status rfsn_paged_attention_peer(const rfsn_arena* arena,
+                                               const float* q, int batch, int q_heads, int kv_heads,
+                                               int q_len, int q_pos0,
+                                               const rfsn_page_table* table,
+                                               const rfsn_hot_window* hot,
+                                               rfsn_peer_group* peers,
+                                               float* out, float* lse,
+                                               void* workspace, size_t workspace_bytes,
+                                               int max_splits, void* stream);
+
 /* Reads the device error word of a workspace (after synchronising `stream`,
  * bounded by timeout_us) and clears it. RFSN_ERR_DEVICE if a kernel set it. */
 RFSN_API rfsn_status rfsn_workspace_check(void* workspace, void* stream, int64_t timeout_us);

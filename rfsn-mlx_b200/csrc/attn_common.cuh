@@ -143,11 +143,16 @@ struct PagedCursor {
 // (thread 0 included) after the CTA partial has been written. `flag` is a
 // shared int; `sbuf` is shared scratch of merge_scratch_floats() floats.
 __host__ __device__ constexpr int merge_scratch_floats(int nslots, int splits) { return 2 * nslots * splits + 2 * nslots; }
+// (totals holds L then the LSE per slot: 2 * nslots floats)
+
+__device__ __forceinline__ void peer_exchange(const PeerParams& peer, const WsView& ws, int group, int nslots,
+                                              int head_dim, const OutMap& om, int bh, float* out, float* lse,
+                                              const float* my_lse, int* flag, int bar_id, int nthreads);
 
 __device__ __forceinline__ void finish_splits(const WsView& ws, int counter_idx, int part_base, int split_stride,
                                               int splits, int slot0, int nslots, int head_dim, const OutMap& om,
                                               int bh, float* out, float* lse, int* flag, float* sbuf, int bar_id,
-                                              int nthreads) {
+                                              int nthreads, const PeerParams* peer = nullptr) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = nthreads >> 5;
     __threadfence();
     named_barrier_sync(bar_id, nthreads);
@@ -162,7 +167,7 @@ __device__ __forceinline__ void finish_splits(const WsView& ws, int counter_idx,
     }
     float* wts = sbuf;                          // [nslots][splits] m_s, then weights
     float* ls = sbuf + nslots * splits;         // [nslots][splits] l_s
-    float* totals = ls + nslots * splits;       // [nslots] L
+    float* totals = ls + nslots * splits;       // [nslots] L, then [nslots] natural-log LSE
     for (int i = tid; i < nslots * splits; i += nthreads) {
         const int sl = i / splits, s = i - sl * splits;
         const int p = part_base + s * split_stride + slot0 + sl;
@@ -187,7 +192,9 @@ __device__ __forceinline__ void finish_splits(const WsView& ws, int counter_idx,
         for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
         if (lane == 0) {
             totals[sl] = L;
-            if (lse != nullptr) lse[om.row(bh, slot0 + sl)] = (L > 0.f) ? (M + log2f(L)) * 0.69314718055994531f : -CUDART_INF_F;
+            const float my_lse = (L > 0.f) ? (M + log2f(L)) * 0.69314718055994531f : -CUDART_INF_F;
+            totals[nslots + sl] = my_lse;
+            if (lse != nullptr && peer == nullptr) lse[om.row(bh, slot0 + sl)] = my_lse;
         }
     }
     named_barrier_sync(bar_id, nthreads);
@@ -239,6 +246,95 @@ __device__ __forceinline__ void finish_splits(const WsView& ws, int counter_idx,
         }
     }
     if (splits > 1 && tid == 0) ws.counters[counter_idx] = 0;
+    if (peer != nullptr) {
+        named_barrier_sync(bar_id, nthreads);
+        peer_exchange(*peer, ws, bh, nslots, head_dim, om, bh, out, lse, totals + nslots, flag, bar_id, nthreads);
+    }
+}
+
+// Fused cross-GPU merge, run by the last CTA of `group` on every rank after
+// its local result (out rows of the group's slots, `my_lse`) is final:
+//  1. bump this rank's call counter c for the group (parity c & 1 selects the
+//     mailbox half, so a rank one call ahead never overwrites a part that a
+//     peer has not merged yet: finishing call c needs every peer's part c);
+//  2. store the rows + LSE into every rank's mailbox (NVLink stores for
+//     peers), fence at system scope, publish c in every rank's flags with a
+//     release store;
+//  3. wait (bounded by peer.timeout_ns) until every source published >= c in
+//     the local flags (acquire loads);
+//  4. LSE-merge the P parts in rank order and overwrite out (and lse).
+__device__ __forceinline__ void peer_exchange(const PeerParams& peer, const WsView& ws, int group, int nslots,
+                                              int head_dim, const OutMap& om, int bh, float* out, float* lse,
+                                              const float* my_lse, int* flag, int bar_id, int nthreads) {
+    const int tid = threadIdx.x;
+    const int P = peer.world;
+    const int stride = head_dim + 4;                 // floats per slot in a part
+    const int part_floats = kPeerSlots * stride;     // floats per (source, group)
+    if (tid == 0) {
+        const int c = peer.calls[group] + 1;
+        peer.calls[group] = c;
+        *flag = c;
+    }
+    named_barrier_sync(bar_id, nthreads);
+    const int c = *flag;
+    const int groups = (int)gridDim.y;  // grid = splits x groups
+    const size_t half = (size_t)kMaxPeers * groups * part_floats;
+    const size_t mine = (size_t)(c & 1) * half + ((size_t)peer.rank * groups + group) * part_floats;
+    // 2. scatter this rank's part to every rank
+    const int d4n = head_dim >> 2;
+    for (int idx = tid; idx < P * nslots * d4n; idx += nthreads) {
+        const int r = idx / (nslots * d4n);
+        const int rem = idx - r * nslots * d4n;
+        const int sl = rem / d4n, d4 = rem - sl * d4n;
+        const float4 v = *reinterpret_cast<const float4*>(out + om.row(bh, sl) * head_dim + 4 * d4);
+        *reinterpret_cast<float4*>(peer.parts[r] + mine + (size_t)sl * stride + 4 * d4) = v;
+    }
+    for (int idx = tid; idx < P * nslots; idx += nthreads) {
+        const int r = idx / nslots, sl = idx - r * nslots;
+        peer.parts[r][mine + (size_t)sl * stride + head_dim] = my_lse[sl];
+    }
+    __threadfence_system();
+    named_barrier_sync(bar_id, nthreads);
+    if (tid < P) st_release_sys(peer.flags[tid] + (size_t)peer.rank * groups + group, c);
+    // 3. wait for every source
+    if (tid < P) {
+        const int* f = peer.flags[peer.rank] + (size_t)tid * groups + group;
+        const long long t0 = global_ns();
+        while (ld_acquire_sys(f) < c) {
+            if (global_ns() - t0 > peer.timeout_ns) {
+                atomicExch(ws.error, kDevErrPeerTimeout);
+                break;
+            }
+            __nanosleep(64);
+        }
+    }
+    named_barrier_sync(bar_id, nthreads);
+    // 4. merge the P parts (local mailbox, bypassing L1: peers wrote it)
+    const float* base = peer.parts[peer.rank] + (size_t)(c & 1) * half + (size_t)group * part_floats;
+    const size_t src_stride = (size_t)groups * part_floats;
+    for (int idx = tid; idx < nslots * d4n; idx += nthreads) {
+        const int sl = idx / d4n, d4 = idx - sl * d4n;
+        float M = -CUDART_INF_F;
+        for (int r = 0; r < P; ++r) M = fmaxf(M, __ldcv(base + r * src_stride + (size_t)sl * stride + head_dim));
+        float W = 0.f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (M != -CUDART_INF_F) {
+            for (int r = 0; r < P; ++r) {
+                const float* pr = base + r * src_stride + (size_t)sl * stride;
+                const float w = expf(__ldcv(pr + head_dim) - M);
+                const float4 v = __ldcv(reinterpret_cast<const float4*>(pr + 4 * d4));
+                W += w;
+                acc.x += w * v.x;
+                acc.y += w * v.y;
+                acc.z += w * v.z;
+                acc.w += w * v.w;
+            }
+        }
+        const float inv = W > 0.f ? 1.f / W : 0.f;
+        *reinterpret_cast<float4*>(out + om.row(bh, sl) * head_dim + 4 * d4) =
+            make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+        if (lse != nullptr && d4 == 0) lse[om.row(bh, sl)] = W > 0.f ? M + logf(W) : -CUDART_INF_F;
+    }
 }
 
 }  // namespace rfsn

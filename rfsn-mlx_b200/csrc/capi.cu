@@ -40,17 +40,6 @@ rfsn_status cuda_status(cudaError_t e, const char* what) {
 
 using namespace rfsn;
 
-struct rfsn_arena {
-    void* k;
-    void* v;
-    int dtype;
-    int groups;
-    int rows;
-    int head_dim;
-    int device;
-    bool has_tma;
-    CUtensorMap maps[4];  // K 64-row box, V 64-row box, K 8-row box, V 8-row box
-};
 
 namespace {
 
@@ -368,6 +357,16 @@ extern "C" {
 rfsn_status rfsn_paged_attention(const rfsn_arena* arena, const float* q, int batch, int q_heads, int kv_heads, int q_len,
                                  int q_pos0, const rfsn_page_table* table, const rfsn_hot_window* hot, float* out,
                                  float* lse, void* workspace, size_t workspace_bytes, int max_splits, void* stream) {
+    return rfsn::paged_attention_impl(arena, q, batch, q_heads, kv_heads, q_len, q_pos0, table, hot, out, lse, workspace,
+                                      workspace_bytes, max_splits, nullptr, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"
+
+rfsn_status rfsn::paged_attention_impl(const rfsn_arena* arena, const float* q, int batch, int q_heads, int kv_heads,
+                                       int q_len, int q_pos0, const rfsn_page_table* table, const rfsn_hot_window* hot,
+                                       float* out, float* lse, void* workspace, size_t workspace_bytes, int max_splits,
+                                       const PeerParams* peer, cudaStream_t s) {
     RFSN_CHECK_ARG(arena != nullptr && table != nullptr && hot != nullptr, "rfsn_paged_attention: NULL arena/table/hot");
     CommonArgs a;
     rfsn_status st = check_common(q, batch, q_heads, kv_heads, q_len, arena->head_dim, out, workspace, &a);
@@ -383,13 +382,17 @@ rfsn_status rfsn_paged_attention(const rfsn_arena* arena, const float* q, int ba
     const int first = hot->length < hot->capacity - hot->head_index ? hot->length : hot->capacity - hot->head_index;
     const int hot_tiles = (first + kTile - 1) / kTile + (hot->length - first + kTile - 1) / kTile;
     const int total_tiles = table->archived_tiles + hot_tiles;
-    if (total_tiles <= 0) {
+    if (total_tiles <= 0 && peer == nullptr) {
         set_error("run_segmented_attention requires at least one KV segment");
         return RFSN_ERR_INVALID_ARG;
     }
     const int sms = sm_count_cached();
     const bool use_fast = arena->has_tma && arena->head_dim == 128 && a.nslots <= 4;
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (peer != nullptr && !use_fast) {
+        set_error("fused cross-GPU merge needs the tensor-core decode shape (bf16/f16, head_dim 128, <= 4 query "
+                  "slots per KV head)");
+        return RFSN_ERR_UNSUPPORTED;
+    }
     if (use_fast) {
         fast::Params p;
         int splits, tps;
@@ -425,6 +428,8 @@ rfsn_status rfsn_paged_attention(const rfsn_arena* arena, const float* q, int ba
         p.qscale = qscale_for(128);
         p.pscale = arena->dtype == RFSN_F16 ? 4096.f : 1.f;
         p.ws = ws_view(workspace, w);
+        memset(&p.peer, 0, sizeof(p.peer));
+        if (peer != nullptr) p.peer = *peer;
         return fast_launch(arena->dtype, arena->maps, p, kFastStages, s);
     }
     generic::Params p;
@@ -468,6 +473,8 @@ rfsn_status rfsn_paged_attention(const rfsn_arena* arena, const float* q, int ba
     p.hstart = hot->start_pos;
     return generic_launch(arena->dtype, true, p, a.groups, s);
 }
+
+extern "C" {
 
 rfsn_status rfsn_segmented_attention(const float* q, int batch, int q_heads, int kv_heads, int q_len, int q_pos0,
                                      int head_dim, int kv_dtype, const rfsn_segment_desc* segments, int n_segments,

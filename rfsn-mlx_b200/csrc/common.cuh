@@ -233,6 +233,41 @@ inline WsView ws_view(void* base, const WsLayout& w) {
 constexpr int kDevErrTimeout = 1;
 constexpr int kDevErrBadTable = 2;  // a page-table record points outside the arena
 
+// Cross-GPU exchange of the fused sharded merge (see peer.cu). Each rank owns
+// a mailbox in its HBM that every peer maps with CUDA IPC:
+//   flags  int32 [kMaxPeers][groups]         call counter last published by each source
+//   calls  int32 [groups]                    this rank's own call counter per group
+//   parts  float [2][kMaxPeers][groups][kPeerSlots][head_dim + 4]
+//          (parity of the call, source rank, group, query slot; out then lse)
+constexpr int kMaxPeers = 8;
+constexpr int kPeerSlots = 4;
+constexpr int kDevErrPeerTimeout = 3;
+
+struct PeerParams {
+    int world;                     // 0: no cross-GPU merge
+    int rank;
+    float* parts[kMaxPeers];       // every rank's parts region (own one included)
+    int* flags[kMaxPeers];         // every rank's flags region
+    int* calls;                    // own call counters
+    long long timeout_ns;          // bounded wait for peers
+};
+
+__device__ __forceinline__ long long global_ns() {
+    long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+    asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+    int v;
+    asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
 // Output addressing: slot j of kv group (b, hk) is query row r = j / G of q
 // head hk * G + j % G (GQA head mapping of layer.py:140-150).
 struct OutMap {

@@ -331,7 +331,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
     // The split merge reuses red_o as scratch once every consumer thread is past
     // the reads above (finish_splits starts with a barrier).
     finish_splits(p.ws, bh, part_base, SLOTS, p.splits, 0, p.nslots, D, om, bh, p.out, p.lse, &sm.flag,
-                  &sm.red_o[0][0][0], 1, NCW * 32);
+                  &sm.red_o[0][0][0], 1, NCW * 32, p.peer.world > 0 ? &p.peer : nullptr);
 }
 
 template <typename T, int STAGES>

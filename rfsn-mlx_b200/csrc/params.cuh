@@ -4,6 +4,19 @@
 
 #include "common.cuh"
 
+// One layer's K/V arena and its TMA descriptors (opaque to C ABI users).
+struct rfsn_arena {
+    void* k;
+    void* v;
+    int dtype;
+    int groups;
+    int rows;
+    int head_dim;
+    int device;
+    bool has_tma;
+    CUtensorMap maps[4];  // K 64-row box, V 64-row box, K 8-row box, V 8-row box
+};
+
 namespace rfsn {
 namespace fast {
 struct Params {
@@ -19,6 +32,7 @@ struct Params {
     float qscale;             // 1/sqrt(D) * log2(e)
     float pscale;             // power-of-two scale applied to p before the 16-bit split
     WsView ws;
+    PeerParams peer;          // world == 0: local result only
 };
 }  // namespace fast
 
@@ -49,6 +63,11 @@ int fast_max_splits();
 rfsn_status fast_launch(int dtype, const CUtensorMap* maps, const fast::Params& p, int stages, cudaStream_t stream);
 // generic_attn.cu
 rfsn_status generic_launch(int dtype, bool paged, const generic::Params& p, int groups, cudaStream_t stream);
+// capi.cu: shared body of the paged-attention entry points (peer may be NULL)
+rfsn_status paged_attention_impl(const rfsn_arena* arena, const float* q, int batch, int q_heads, int kv_heads,
+                                 int q_len, int q_pos0, const rfsn_page_table* table, const rfsn_hot_window* hot,
+                                 float* out, float* lse, void* workspace, size_t workspace_bytes, int max_splits,
+                                 const PeerParams* peer, cudaStream_t stream);
 // merge.cu
 rfsn_status lse_merge_launch(const float* parts_out, const float* parts_lse, int n_parts, int rows, int head_dim,
                              float* out, float* lse_out, cudaStream_t stream);

@@ -57,6 +57,12 @@ EXPORTED_SYMBOLS = (
     "rfsn_workspace_check",
     "rfsn_launch_count",
     "rfsn_paged_attention_noalloc",
+    "rfsn_peer_ipc_handle_bytes",
+    "rfsn_peer_group_create",
+    "rfsn_peer_group_connect",
+    "rfsn_peer_group_set_timeout",
+    "rfsn_peer_group_destroy",
+    "rfsn_paged_attention_peer",
 )
 
 
@@ -144,6 +150,16 @@ def load_library() -> ctypes.CDLL:
         "rfsn_lse_merge": (i32, [vp, vp, i32, i32, i32, vp, vp, vp]),
         "rfsn_workspace_check": (i32, [vp, vp, i64]),
         "rfsn_launch_count": (ctypes.c_uint64, []),
+        "rfsn_peer_ipc_handle_bytes": (i32, []),
+        "rfsn_peer_group_create": (i32, [i32, i32, i32, i32, ctypes.POINTER(vp), vp]),
+        "rfsn_peer_group_connect": (i32, [vp, vp]),
+        "rfsn_peer_group_set_timeout": (i32, [vp, i64]),
+        "rfsn_peer_group_destroy": (i32, [vp]),
+        "rfsn_paged_attention_peer": (
+            i32,
+            [vp, vp, i32, i32, i32, i32, i32, ctypes.POINTER(PageTableC), ctypes.POINTER(HotWindowC), vp, vp, vp, vp,
+             sz, i32, vp],
+        ),
         "rfsn_paged_attention_noalloc": (
             i32,
             [vp, vp, i32, i32, i32, i32, i32, ctypes.POINTER(PageTableC), ctypes.POINTER(HotWindowC), vp, vp, i32, vp],

@@ -776,8 +776,15 @@ class LayerKVCache:
 
 
 def paged_attention(cache: LayerKVCache, q: torch.Tensor, q_start_pos: int, segments: PagedSegments,
-                    *, want_lse: bool = False, max_splits: int = 0, workspace: Optional[native.Workspace] = None):
-    if len(segments) == 0:
+                    *, want_lse: bool = False, max_splits: int = 0, workspace: Optional[native.Workspace] = None,
+                    peers: Optional[Any] = None):
+    """Exact attention of q over a layer's page table + hot window.
+
+    With ``peers`` (a ``sharded.PeerGroup``) the kernel also merges the
+    results of every rank of the group over NVLink, so the returned output is
+    the attention over the whole sharded context (an empty local shard is
+    allowed then)."""
+    if len(segments) == 0 and peers is None:
         raise RuntimeError("run_segmented_attention requires at least one KV segment")
     if q.dim() != 4 or q.shape[0] != cache.batch_size or q.shape[3] != cache.config.head_dim:
         raise ValueError(f"q must be [batch={cache.batch_size}, heads, q_len, head_dim={cache.config.head_dim}]")
@@ -801,6 +808,17 @@ def paged_attention(cache: LayerKVCache, q: torch.Tensor, q_start_pos: int, segm
     ws = workspace if workspace is not None else native.default_workspace(cache.device)
     nbytes = native.workspace_bytes(B, H, cache.num_kv_heads, Lq, D, max_splits)
     buf = ws.get(nbytes)
+    if peers is not None:
+        native.check(
+            native.lib().rfsn_paged_attention_peer(
+                cache.arena.handle, qf.data_ptr(), B, H, cache.num_kv_heads, Lq, int(q_start_pos),
+                native.ctypes.byref(table), native.ctypes.byref(hot), peers.handle, out.data_ptr(),
+                lse.data_ptr() if lse is not None else None, buf.data_ptr(), buf.numel(), max_splits,
+                native.stream_ptr(),
+            ),
+            "rfsn_paged_attention_peer",
+        )
+        return (out, lse) if want_lse else out
     native.check(
         native.lib().rfsn_paged_attention(
             cache.arena.handle, qf.data_ptr(), B, H, cache.num_kv_heads, Lq, int(q_start_pos),

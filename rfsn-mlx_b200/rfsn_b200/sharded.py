@@ -8,14 +8,22 @@ two passes). Rank r of P holds the archived blocks
 also holds the hot window; no rank reads another rank's K/V.
 
 A decode step on every rank: rotate q (the rank that owns the hot window also
-appends the new token's K/V), attend over the local blocks with the paged
-kernel, which also returns the natural-log LSE of each query row, all-gather
-the (output, LSE) pairs (fp32, ~16.6 KB per rank for 32 heads x 128) with
-NCCL, and combine them in rank order with ``rfsn_lse_merge``.
+appends the new token's K/V), attend over the local blocks, and combine the
+ranks' (output, LSE) pairs in rank order. Two exchange paths:
+
+* ``PeerGroup`` (default for the tensor-core decode shape): the merge is fused
+  into the attention kernel. Each rank's mailbox is mapped into every peer
+  with CUDA IPC; the last CTA of each KV head stores its part into every
+  mailbox over NVLink, waits (bounded) for the peers' parts and merges them,
+  so one kernel per step produces the merged result on every rank.
+* NCCL: the paged kernel returns (output, LSE), ``gather_parts`` all-gathers
+  them (fp32, ~16.6 KB per rank for 32 heads x 128) and ``rfsn_lse_merge``
+  combines them.
 """
 
 from __future__ import annotations
 
+import ctypes
 from typing import Optional
 
 import torch
@@ -73,16 +81,68 @@ def merge_across_ranks(out: torch.Tensor, lse: torch.Tensor, group: Optional[dis
     return merge_parts(parts_out, parts_lse, out.shape)
 
 
+class PeerGroup:
+    """NVLink mailboxes of one sharded layer shape (batch * kv_heads groups,
+    head_dim) across the ranks of ``group`` (one process per GPU).
+
+    Collective to construct and to close: every rank must create it, and
+    closing waits on a barrier so no peer still writes into a mailbox that is
+    being released."""
+
+    def __init__(self, groups: int, head_dim: int, group: Optional[dist.ProcessGroup] = None,
+                 timeout_s: float = 2.0) -> None:
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        lib = native.lib()
+        nbytes = lib.rfsn_peer_ipc_handle_bytes()
+        mine = (ctypes.c_ubyte * nbytes)()
+        handle = ctypes.c_void_p()
+        native.check(lib.rfsn_peer_group_create(self.world, self.rank, groups, head_dim, ctypes.byref(handle), mine),
+                     "rfsn_peer_group_create")
+        self.handle = handle
+        raw = bytes(mine)
+        if self.world > 1:
+            t = torch.tensor(list(raw), dtype=torch.uint8, device=torch.device("cuda", torch.cuda.current_device()))
+            if dist.get_backend(group) == "nccl":
+                out = torch.empty(self.world * nbytes, dtype=torch.uint8, device=t.device)
+                dist.all_gather_into_tensor(out, t, group=group)
+            else:
+                parts = [torch.empty_like(t) for _ in range(self.world)]
+                dist.all_gather(parts, t, group=group)
+                out = torch.cat(parts)
+            raw = bytes(out.cpu().numpy().tobytes())
+        table = (ctypes.c_ubyte * len(raw)).from_buffer_copy(raw)
+        native.check(lib.rfsn_peer_group_connect(self.handle, table), "rfsn_peer_group_connect")
+        native.check(lib.rfsn_peer_group_set_timeout(self.handle, int(timeout_s * 1e6)), "rfsn_peer_group_set_timeout")
+        if self.world > 1:
+            dist.barrier(group=group)
+
+    def close(self) -> None:
+        if self.handle:
+            torch.cuda.synchronize()
+            if self.world > 1:
+                dist.barrier(group=self.group)
+            native.lib().rfsn_peer_group_destroy(self.handle)
+            self.handle = ctypes.c_void_p()
+
+
 def sharded_decode_step(cache: LayerKVCache, q: torch.Tensor, k: Optional[torch.Tensor], v: Optional[torch.Tensor],
-                        pos: int, *, owns_hot: bool, group: Optional[dist.ProcessGroup] = None) -> torch.Tensor:
+                        pos: int, *, owns_hot: bool, group: Optional[dist.ProcessGroup] = None,
+                        peers: Optional[PeerGroup] = None) -> torch.Tensor:
     """One decode token of one layer on this rank's shard; returns the merged
-    float32 output [B, H, 1, D] on every rank."""
+    float32 output [B, H, 1, D] on every rank. With ``peers`` the merge is
+    fused into the attention kernel (NVLink); otherwise it goes through NCCL."""
     if owns_hot:
         cache.evict_for_append(int(k.shape[2]))
         q_rot = cache.append_rope(q, k, v, pos)
     else:
         q_rot = cache.rope_query(q, pos)
     segments = cache.get_attention_segments()
+    if peers is not None:
+        from .cache import paged_attention
+
+        return paged_attention(cache, q_rot, pos, segments, peers=peers)
     if len(segments) == 0:
         # a rank with nothing to attend contributes an empty part (lse = -inf)
         out = torch.zeros(q_rot.shape, dtype=torch.float32, device=q_rot.device)

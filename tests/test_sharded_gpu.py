@@ -92,13 +92,39 @@ def test_emulated_ranks_merge_to_unsharded_result(world):
     np.testing.assert_allclose(merged.cpu().numpy(), full.cpu().numpy(), atol=1e-5)
 
 
+def test_peer_group_of_one_matches_local_attention():
+    """The fused-merge kernel path with a single rank: its mailbox exchange
+    (store, release flag, acquire wait, merge) must reproduce the local result
+    on consecutive calls (both mailbox halves)."""
+    import torch
+
+    from rfsn_b200.cache import paged_attention
+    from rfsn_b200.sharded import PeerGroup
+
+    q, k, v, total = _data()
+    qd = torch.from_numpy(q).cuda()
+    with tempfile.TemporaryDirectory() as tmp:
+        cache = _shard_cache(0, 1, k, v, torch.device("cuda", 0), tmp)
+        segs = cache.get_attention_segments()
+        ref, ref_lse = paged_attention(cache, qd, total - 1, segs, want_lse=True)
+        peers = PeerGroup(1 * HKV, D)
+        for _ in range(3):
+            out, lse = paged_attention(cache, qd, total - 1, segs, want_lse=True, peers=peers)
+            np.testing.assert_allclose(out.cpu().numpy(), ref.cpu().numpy(), atol=1e-6)
+            np.testing.assert_allclose(lse.cpu().numpy(), ref_lse.cpu().numpy(), atol=1e-5)
+        from rfsn_b200 import _native as native
+
+        native.default_workspace(torch.device("cuda", 0)).check()
+        peers.close()
+
+
 def _port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         return s.getsockname()[1]
 
 
-def _nccl_worker(rank, world, port, results):
+def _nccl_worker(rank, world, port, results, mode="nccl"):
     try:
         import sys
 
@@ -107,7 +133,8 @@ def _nccl_worker(rank, world, port, results):
         import torch
         import torch.distributed as dist
 
-        from rfsn_b200.sharded import sharded_decode_step
+        from rfsn_b200.cache import paged_attention
+        from rfsn_b200.sharded import PeerGroup, sharded_decode_step
 
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
         torch.cuda.set_device(rank)
@@ -127,9 +154,21 @@ def _nccl_worker(rank, world, port, results):
             import torch as T
 
             bf = lambda x: T.from_numpy(np.ascontiguousarray(x)).to(T.bfloat16).cuda()  # noqa: E731
+            peers = PeerGroup(HKV, D) if mode == "p2p" else None
             out = sharded_decode_step(cache, bf(q), bf(k[:, :, -1:]) if owner else None,
-                                      bf(v[:, :, -1:]) if owner else None, total - 1, owns_hot=owner)
-            results.put((rank, out.cpu().numpy()))
+                                      bf(v[:, :, -1:]) if owner else None, total - 1, owns_hot=owner, peers=peers)
+            outs = [out.cpu().numpy()]
+            if peers is not None:
+                # more calls on the same context: alternate mailbox halves, same result
+                q_rot = cache.rope_query(bf(q), total - 1)
+                for _ in range(3):
+                    outs.append(paged_attention(cache, q_rot, total - 1, cache.get_attention_segments(),
+                                                peers=peers).cpu().numpy())
+                from rfsn_b200 import _native as native
+
+                native.default_workspace(torch.device("cuda", rank)).check()
+                peers.close()
+            results.put((rank, outs))
         dist.barrier()
         dist.destroy_process_group()
     except Exception:
@@ -137,7 +176,8 @@ def _nccl_worker(rank, world, port, results):
 
 
 @pytest.mark.skipif("not __import__('torch').cuda.device_count() >= 2", reason="needs 2 GPUs")
-def test_nccl_sharded_decode_step_two_gpus():
+@pytest.mark.parametrize("mode", ["nccl", "p2p"])
+def test_sharded_decode_step_two_gpus(mode):
     import torch
 
     from oracle.rope import apply_rope, rope_tables
@@ -146,7 +186,7 @@ def test_nccl_sharded_decode_step_two_gpus():
     ctx = mp.get_context("spawn")
     results = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_nccl_worker, args=(r, world, port, results)) for r in range(world)]
+    procs = [ctx.Process(target=_nccl_worker, args=(r, world, port, results, mode)) for r in range(world)]
     for p in procs:
         p.start()
     got = dict(results.get(timeout=300) for _ in range(world))
@@ -164,4 +204,5 @@ def test_nccl_sharded_decode_step_two_gpus():
 
     ref = run_segmented_attention(q_rot, [(k_ctx, r(v), 0)], total - 1, grouped=True)
     for rank in range(world):
-        assert float(np.abs(got[rank] - ref).max()) <= 2e-3
+        for out in got[rank]:
+            assert float(np.abs(out - ref).max()) <= 2e-3
