@@ -11,10 +11,12 @@ q, K, V ~ N(0, 1) (seeded). One "call" is one decode-attention call (1 new
 token, all heads, whole context); a step is ``calls_per_step`` back-to-back
 calls. The metric unit is calls/s (= decoded tokens/s for this layer).
 
-With N GPUs (torchrun, one process per GPU, NCCL) the archived blocks are
-partitioned contiguously over the ranks and the hot ring sits on the last
-rank; each call attends locally and merges the ranks' (output, LSE) pairs with
-an NCCL all-gather + LSE-merge kernel (strong scaling: the context is fixed).
+With N GPUs (torchrun, one process per GPU) the archived blocks are
+partitioned contiguously over the ranks, balancing tokens with the hot ring on
+the last rank; each call attends locally and the ranks' (output, LSE) pairs
+are merged inside the attention kernel over NVLink (``--merge p2p``, default)
+or with an NCCL all-gather + LSE-merge kernel (``--merge nccl``). Strong
+scaling: the context is fixed.
 
 Reported (rank 0, one JSON line): device throughput with inputs resident in
 HBM (CUDA-graph-captured calls timed with CUDA events, max over ranks),
@@ -151,10 +153,10 @@ def build_shard(w: dict, rank: int, world: int, device, extra_tokens: int):
     import torch
 
     from rfsn_b200 import LayerKVCache, RFSNConfig
-    from rfsn_b200.sharded import shard_range
+    from rfsn_b200.sharded import balanced_shards
 
     blocks = w["blocks"]
-    lo, hi = shard_range(len(blocks), rank, world)
+    lo, hi = balanced_shards(blocks, w["hot"], world)[rank]
     starts = [sum(blocks[:i]) for i in range(len(blocks))]
     archived_total = sum(blocks)
     local_tokens = sum(blocks[lo:hi])

@@ -94,6 +94,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
         }
         if (lane == 0 && ntiles > 0) {
             const int row_base = bh * p.rows;
+            bool waited = false;
             for (int it = 0; it < ntiles; ++it) {
                 const int s = it % STAGES;
                 if (it >= STAGES) {
@@ -104,6 +105,11 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
                     }
                 }
                 TileRef t = cur.current();
+                if (!waited && t.span >= p.n_blocks) {
+                    // hot-window rows may be written by the kernel this one overlaps (ring append)
+                    griddep_wait();
+                    waited = true;
+                }
                 if (t.row < 0 || t.row + t.nvalid > p.rows) {
                     // corrupt record: flag it and stream nothing useful (keys masked out)
                     atomicExch(p.ws.error, kDevErrBadTable);
@@ -144,6 +150,9 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
 
     // Q^T operand fragments: column n = g holds slot n & 3; n < 4 the 16-bit
     // head of q*qscale, n >= 4 the 16-bit remainder.
+    // q (and the workspace written later) may come from the kernel this one
+    // overlaps under programmatic dependent launch: wait for it first.
+    griddep_wait();
     uint32_t qf[8][2];
     {
         const int slot = g & 3;
@@ -268,6 +277,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
         if (lane == 0) mbar_arrive(&sm.empty[s]);
     }
 
+    griddep_launch_dependents();
     if (sm.abort) {
         // Drain: wait (bounded) for loads already issued into stages we did not consume.
         for (int it = consumed; it < min(ntiles, consumed + STAGES); ++it) {
@@ -339,9 +349,17 @@ rfsn_status launch(const CUtensorMap* maps, const Params& p, cudaStream_t stream
     const size_t smem = sizeof(Smem<STAGES>) + 1024;
     auto kern = paged_decode_kernel<T, STAGES>;
     RFSN_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    dim3 grid(p.splits, p.groups);
-    kern<<<grid, NTHREADS, smem, stream>>>(maps[0], maps[1], maps[2], maps[3], p);
-    RFSN_CUDA(cudaGetLastError());
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.splits, p.groups);
+    cfg.blockDim = dim3(NTHREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    RFSN_CUDA(cudaLaunchKernelEx(&cfg, kern, maps[0], maps[1], maps[2], maps[3], p));
     note_launch();
     return RFSN_OK;
 }

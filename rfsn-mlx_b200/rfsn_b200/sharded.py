@@ -38,6 +38,27 @@ def shard_range(n_blocks: int, rank: int, world: int) -> tuple[int, int]:
     return n_blocks * rank // world, n_blocks * (rank + 1) // world
 
 
+def balanced_shards(block_lens: list[int], hot_len: int, world: int) -> list[tuple[int, int]]:
+    """Contiguous block ranges [lo, hi) per rank (page-table order) that
+    balance tokens, counting the hot window on the last rank: each rank's
+    range ends at the block boundary closest to its share of the total."""
+    total = sum(block_lens) + hot_len
+    cum = [0]
+    for n in block_lens:
+        cum.append(cum[-1] + n)
+    bounds = [0]
+    for r in range(1, world):
+        target = total * r / world
+        # boundary index b in [bounds[-1], len(block_lens)] with cum[b] closest to target
+        best = bounds[-1]
+        for b in range(bounds[-1], len(block_lens) + 1):
+            if abs(cum[b] - target) < abs(cum[best] - target):
+                best = b
+        bounds.append(best)
+    bounds.append(len(block_lens))
+    return [(bounds[r], bounds[r + 1]) for r in range(world)]
+
+
 def gather_parts(out: torch.Tensor, lse: torch.Tensor, group: Optional[dist.ProcessGroup] = None):
     """All-gather every rank's (out [B,H,Lq,D], lse [B,H,Lq]) in rank order.
 

@@ -103,6 +103,18 @@ def test_rank_that_never_joins_is_detected_on_the_host():
     assert isinstance(got[0], str) and got[0].startswith("error"), got[0]
 
 
+def test_balanced_shards_are_contiguous_and_balanced():
+    from rfsn_b200.sharded import balanced_shards
+
+    blocks = [1000] * 127 + [1024]
+    for world in (1, 2, 4, 8):
+        ranges = balanced_shards(blocks, 4096, world)
+        assert ranges[0][0] == 0 and ranges[-1][1] == len(blocks)
+        assert all(a[1] == b[0] for a, b in zip(ranges, ranges[1:]))
+        loads = [sum(blocks[lo:hi]) + (4096 if r == world - 1 else 0) for r, (lo, hi) in enumerate(ranges)]
+        assert max(loads) - min(loads) <= 1024 + 24
+
+
 def test_shard_ranges_partition_blocks_contiguously():
     from rfsn_b200.sharded import shard_range
 
