@@ -145,14 +145,76 @@ struct PagedCursor {
 __host__ __device__ constexpr int merge_scratch_floats(int nslots, int splits) { return 2 * nslots * splits + 2 * nslots; }
 // (totals holds L then the LSE per slot: 2 * nslots floats)
 
-__device__ __forceinline__ void peer_exchange(const PeerParams& peer, const WsView& ws, int group, int nslots,
-                                              int head_dim, const OutMap& om, int bh, float* out, float* lse,
-                                              const float* my_lse, int* flag, int bar_id, int nthreads);
+// Fused cross-GPU merge of one float4 of one query slot (called by the last
+// CTA of a group in every rank, one thread per (slot, 4 output columns)):
+// the rank's final local value r (and its LSE) is stamped with the call
+// number and stored into the same place of every rank's mailbox (NVLink
+// stores for peers), then the thread polls the P sources' words for the same
+// place until all carry this call's stamp (bounded by peer.timeout_ns) and
+// merges them in rank order:  out = sum_r e^(lse_r - M) O_r / sum_r e^(lse_r - M).
+// Mailbox halves alternate with the call parity: a rank cannot publish call
+// c + 2 before every peer has published (so finished reading) call c + 1.
+__device__ __forceinline__ void peer_store_and_merge(const PeerParams& peer, const WsView& ws, int call, int group,
+                                                     int sl, int d4, int head_dim, float4 r, float my_lse,
+                                                     const OutMap& om, float* out, float* lse) {
+    const int P = peer.world;
+    const int groups = (int)gridDim.y;  // grid = splits x groups
+    const size_t slot_words = (size_t)head_dim + 2;
+    const size_t half = (size_t)kMaxPeers * groups * kPeerSlots * slot_words;
+    const uint32_t stamp = (uint32_t)call;
+    const size_t src_off = (size_t)(call & 1) * half + (((size_t)peer.rank * groups + group) * kPeerSlots + sl) * slot_words;
+    for (int d = 0; d < P; ++d) {
+        uint2* w = peer.words[d] + src_off;
+        st_volatile_v4(w + 4 * d4, __float_as_uint(r.x), stamp, __float_as_uint(r.y), stamp);
+        st_volatile_v4(w + 4 * d4 + 2, __float_as_uint(r.z), stamp, __float_as_uint(r.w), stamp);
+        if (d4 == 0) st_volatile_v4(w + head_dim, __float_as_uint(my_lse), stamp, 0u, stamp);
+    }
+    const uint2* local = peer.words[peer.rank] + (size_t)(call & 1) * half + ((size_t)group * kPeerSlots + sl) * slot_words;
+    const size_t src_stride = (size_t)groups * kPeerSlots * slot_words;
+    const long long t0 = global_ns();
+    bool timed_out = false;
+    // online merge in rank order: running max M, weight sum W, weighted sum acc
+    float M = -CUDART_INF_F, W = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int src = 0; src < P; ++src) {
+        const uint2* w = local + src * src_stride;
+        uint4 a, b, l;
+        for (;;) {
+            a = ld_volatile_v4(w + 4 * d4);
+            b = ld_volatile_v4(w + 4 * d4 + 2);
+            l = ld_volatile_v4(w + head_dim);
+            if (a.y == stamp && a.w == stamp && b.y == stamp && b.w == stamp && l.y == stamp) break;
+            if (timed_out || global_ns() - t0 > peer.timeout_ns) {
+                timed_out = true;
+                break;
+            }
+            __nanosleep(20);
+        }
+        const float ls = __uint_as_float(l.x);
+        if (ls == -CUDART_INF_F) continue;  // a part that saw no visible key
+        const float4 v = make_float4(__uint_as_float(a.x), __uint_as_float(a.z), __uint_as_float(b.x), __uint_as_float(b.z));
+        if (ls > M) {
+            const float sc = (M == -CUDART_INF_F) ? 0.f : expf(M - ls);
+            W = W * sc + 1.f;
+            acc = make_float4(acc.x * sc + v.x, acc.y * sc + v.y, acc.z * sc + v.z, acc.w * sc + v.w);
+            M = ls;
+        } else {
+            const float wgt = expf(ls - M);
+            W += wgt;
+            acc = make_float4(acc.x + wgt * v.x, acc.y + wgt * v.y, acc.z + wgt * v.z, acc.w + wgt * v.w);
+        }
+    }
+    if (timed_out) atomicExch(ws.error, kDevErrPeerTimeout);
+    const float inv = W > 0.f ? 1.f / W : 0.f;
+    *reinterpret_cast<float4*>(out + om.row(group, sl) * head_dim + 4 * d4) =
+        make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+    if (lse != nullptr && d4 == 0) lse[om.row(group, sl)] = W > 0.f ? M + logf(W) : -CUDART_INF_F;
+}
 
 __device__ __forceinline__ void finish_splits(const WsView& ws, int counter_idx, int part_base, int split_stride,
                                               int splits, int slot0, int nslots, int head_dim, const OutMap& om,
                                               int bh, float* out, float* lse, int* flag, float* sbuf, int bar_id,
-                                              int nthreads, const PeerParams* peer = nullptr) {
+                                              int nthreads, const PeerParams* peer = nullptr, int call = 0) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = nthreads >> 5;
     __threadfence();
     named_barrier_sync(bar_id, nthreads);
@@ -231,7 +293,11 @@ __device__ __forceinline__ void finish_splits(const WsView& ws, int counter_idx,
             }
             const float inv = 1.f / fmaxf(totals[sl], 1e-9f);
             float4 r = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
-            *reinterpret_cast<float4*>(out + om.row(bh, slot0 + sl) * head_dim + 4 * d4) = r;
+            if (peer == nullptr) {
+                *reinterpret_cast<float4*>(out + om.row(bh, slot0 + sl) * head_dim + 4 * d4) = r;
+            } else {
+                peer_store_and_merge(*peer, ws, call, bh, sl, d4, head_dim, r, totals[nslots + sl], om, out, lse);
+            }
         }
     } else {
         for (int idx = tid; idx < nslots * head_dim; idx += nthreads) {
@@ -246,95 +312,7 @@ __device__ __forceinline__ void finish_splits(const WsView& ws, int counter_idx,
         }
     }
     if (splits > 1 && tid == 0) ws.counters[counter_idx] = 0;
-    if (peer != nullptr) {
-        named_barrier_sync(bar_id, nthreads);
-        peer_exchange(*peer, ws, bh, nslots, head_dim, om, bh, out, lse, totals + nslots, flag, bar_id, nthreads);
-    }
-}
-
-// Fused cross-GPU merge, run by the last CTA of `group` on every rank after
-// its local result (out rows of the group's slots, `my_lse`) is final:
-//  1. bump this rank's call counter c for the group (parity c & 1 selects the
-//     mailbox half, so a rank one call ahead never overwrites a part that a
-//     peer has not merged yet: finishing call c needs every peer's part c);
-//  2. store the rows + LSE into every rank's mailbox (NVLink stores for
-//     peers), fence at system scope, publish c in every rank's flags with a
-//     release store;
-//  3. wait (bounded by peer.timeout_ns) until every source published >= c in
-//     the local flags (acquire loads);
-//  4. LSE-merge the P parts in rank order and overwrite out (and lse).
-__device__ __forceinline__ void peer_exchange(const PeerParams& peer, const WsView& ws, int group, int nslots,
-                                              int head_dim, const OutMap& om, int bh, float* out, float* lse,
-                                              const float* my_lse, int* flag, int bar_id, int nthreads) {
-    const int tid = threadIdx.x;
-    const int P = peer.world;
-    const int stride = head_dim + 4;                 // floats per slot in a part
-    const int part_floats = kPeerSlots * stride;     // floats per (source, group)
-    if (tid == 0) {
-        const int c = peer.calls[group] + 1;
-        peer.calls[group] = c;
-        *flag = c;
-    }
-    named_barrier_sync(bar_id, nthreads);
-    const int c = *flag;
-    const int groups = (int)gridDim.y;  // grid = splits x groups
-    const size_t half = (size_t)kMaxPeers * groups * part_floats;
-    const size_t mine = (size_t)(c & 1) * half + ((size_t)peer.rank * groups + group) * part_floats;
-    // 2. scatter this rank's part to every rank
-    const int d4n = head_dim >> 2;
-    for (int idx = tid; idx < P * nslots * d4n; idx += nthreads) {
-        const int r = idx / (nslots * d4n);
-        const int rem = idx - r * nslots * d4n;
-        const int sl = rem / d4n, d4 = rem - sl * d4n;
-        const float4 v = *reinterpret_cast<const float4*>(out + om.row(bh, sl) * head_dim + 4 * d4);
-        *reinterpret_cast<float4*>(peer.parts[r] + mine + (size_t)sl * stride + 4 * d4) = v;
-    }
-    for (int idx = tid; idx < P * nslots; idx += nthreads) {
-        const int r = idx / nslots, sl = idx - r * nslots;
-        peer.parts[r][mine + (size_t)sl * stride + head_dim] = my_lse[sl];
-    }
-    __threadfence_system();
-    named_barrier_sync(bar_id, nthreads);
-    if (tid < P) st_release_sys(peer.flags[tid] + (size_t)peer.rank * groups + group, c);
-    // 3. wait for every source
-    if (tid < P) {
-        const int* f = peer.flags[peer.rank] + (size_t)tid * groups + group;
-        const long long t0 = global_ns();
-        while (ld_acquire_sys(f) < c) {
-            if (global_ns() - t0 > peer.timeout_ns) {
-                atomicExch(ws.error, kDevErrPeerTimeout);
-                break;
-            }
-            __nanosleep(64);
-        }
-    }
-    named_barrier_sync(bar_id, nthreads);
-    // 4. merge the P parts (local mailbox, bypassing L1: peers wrote it)
-    const float* base = peer.parts[peer.rank] + (size_t)(c & 1) * half + (size_t)group * part_floats;
-    const size_t src_stride = (size_t)groups * part_floats;
-    for (int idx = tid; idx < nslots * d4n; idx += nthreads) {
-        const int sl = idx / d4n, d4 = idx - sl * d4n;
-        float M = -CUDART_INF_F;
-        for (int r = 0; r < P; ++r) M = fmaxf(M, __ldcv(base + r * src_stride + (size_t)sl * stride + head_dim));
-        float W = 0.f;
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (M != -CUDART_INF_F) {
-            for (int r = 0; r < P; ++r) {
-                const float* pr = base + r * src_stride + (size_t)sl * stride;
-                const float w = expf(__ldcv(pr + head_dim) - M);
-                const float4 v = __ldcv(reinterpret_cast<const float4*>(pr + 4 * d4));
-                W += w;
-                acc.x += w * v.x;
-                acc.y += w * v.y;
-                acc.z += w * v.z;
-                acc.w += w * v.w;
-            }
-        }
-        const float inv = W > 0.f ? 1.f / W : 0.f;
-        *reinterpret_cast<float4*>(out + om.row(bh, sl) * head_dim + 4 * d4) =
-            make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
-        if (lse != nullptr && d4 == 0) lse[om.row(bh, sl)] = W > 0.f ? M + logf(W) : -CUDART_INF_F;
-    }
+    if (peer != nullptr && tid == 0) peer->calls[bh] = call;
 }
 
 }  // namespace rfsn

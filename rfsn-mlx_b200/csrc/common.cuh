@@ -243,10 +243,14 @@ constexpr int kDevErrBadTable = 2;  // a page-table record points outside the ar
 
 // Cross-GPU exchange of the fused sharded merge (see peer.cu). Each rank owns
 // a mailbox in its HBM that every peer maps with CUDA IPC:
-//   flags  int32 [kMaxPeers][groups]         call counter last published by each source
-//   calls  int32 [groups]                    this rank's own call counter per group
-//   parts  float [2][kMaxPeers][groups][kPeerSlots][head_dim + 4]
-//          (parity of the call, source rank, group, query slot; out then lse)
+//   calls  int32 [groups]   this rank's call counter per group (local only)
+//   words  uint2 [2][kMaxPeers][groups][kPeerSlots][head_dim + 2]
+//          (call parity, source rank, group, query slot; head_dim output
+//          words, the LSE word, one pad word). Each 8-byte word is
+//          {float bits, call stamp}: a receiver knows a word has arrived
+//          when its stamp equals the current call, so data needs no separate
+//          flag and no fence (low-latency "data + flag" words written with
+//          16-byte stores, the scheme NCCL's LL protocol uses).
 constexpr int kMaxPeers = 8;
 constexpr int kPeerSlots = 4;
 constexpr int kDevErrPeerTimeout = 3;
@@ -254,26 +258,29 @@ constexpr int kDevErrPeerTimeout = 3;
 struct PeerParams {
     int world;                     // 0: no cross-GPU merge
     int rank;
-    float* parts[kMaxPeers];       // every rank's parts region (own one included)
-    int* flags[kMaxPeers];         // every rank's flags region
+    uint2* words[kMaxPeers];       // every rank's word region (own one included)
     int* calls;                    // own call counters
     long long timeout_ns;          // bounded wait for peers
 };
+
+__device__ __forceinline__ void st_volatile_v4(uint2* p, uint32_t a, uint32_t fa, uint32_t b, uint32_t fb) {
+    asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(fa), "r"(b), "r"(fb)
+                 : "memory");
+}
+
+__device__ __forceinline__ uint4 ld_volatile_v4(const uint2* p) {
+    uint4 v;
+    asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p)
+                 : "memory");
+    return v;
+}
 
 __device__ __forceinline__ long long global_ns() {
     long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
-}
-
-__device__ __forceinline__ void st_release_sys(int* p, int v) {
-    asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ int ld_acquire_sys(const int* p) {
-    int v;
-    asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
 }
 
 // Output addressing: slot j of kv group (b, hk) is query row r = j / G of q

@@ -51,6 +51,7 @@ struct Smem {
     float red_o[NCW][SLOTS][D];
     int flag;
     int abort;
+    int call;  // cross-GPU merge: this call's stamp for the group
 };
 
 template <typename T, int STAGES>
@@ -153,6 +154,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
     // q (and the workspace written later) may come from the kernel this one
     // overlaps under programmatic dependent launch: wait for it first.
     griddep_wait();
+    if (threadIdx.x == 0) sm.call = p.peer.world > 0 ? p.peer.calls[bh] + 1 : 0;
     uint32_t qf[8][2];
     {
         const int slot = g & 3;
@@ -341,7 +343,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
     // The split merge reuses red_o as scratch once every consumer thread is past
     // the reads above (finish_splits starts with a barrier).
     finish_splits(p.ws, bh, part_base, SLOTS, p.splits, 0, p.nslots, D, om, bh, p.out, p.lse, &sm.flag,
-                  &sm.red_o[0][0][0], 1, NCW * 32, p.peer.world > 0 ? &p.peer : nullptr);
+                  &sm.red_o[0][0][0], 1, NCW * 32, p.peer.world > 0 ? &p.peer : nullptr, sm.call);
 }
 
 template <typename T, int STAGES>

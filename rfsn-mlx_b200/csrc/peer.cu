@@ -4,9 +4,10 @@
 // common.cuh, PeerParams), exports it as a CUDA IPC handle, and maps every
 // peer's mailbox (cudaIpcOpenMemHandle; NVLink peer access is enabled lazily).
 // rfsn_paged_attention_peer then runs the split-KV decode kernel whose last
-// CTA per KV head stores its (output, LSE) into every rank's mailbox and
-// merges the parts of all ranks itself (attn_common.cuh, peer_exchange):
-// no collective library call and no extra kernel per decode step.
+// CTA per KV head stamps its (output, LSE) into every rank's mailbox and
+// merges the parts of all ranks itself (attn_common.cuh,
+// peer_store_and_merge): no collective library call and no extra kernel per
+// decode step.
 #include <cstring>
 #include <vector>
 
@@ -17,7 +18,7 @@ struct rfsn_peer_group {
     int world = 0, rank = 0, groups = 0, head_dim = 0, device = 0;
     void* local = nullptr;          // own mailbox (cudaMalloc)
     size_t bytes = 0;
-    size_t flags_off = 0, calls_off = 0, parts_off = 0;
+    size_t calls_off = 0, words_off = 0;
     std::vector<void*> mapped;      // mailbox base of every rank (own included)
     bool connected = false;
     long long timeout_ns = 2000000000LL;
@@ -26,13 +27,11 @@ struct rfsn_peer_group {
 namespace {
 
 void layout(rfsn_peer_group* g) {
-    const size_t flags = sizeof(int) * (size_t)rfsn::kMaxPeers * g->groups;
     const size_t calls = sizeof(int) * (size_t)g->groups;
-    const size_t parts = sizeof(float) * 2 * (size_t)rfsn::kMaxPeers * g->groups * rfsn::kPeerSlots * (g->head_dim + 4);
-    g->flags_off = 256;
-    g->calls_off = rfsn::align_up(g->flags_off + flags, 256);
-    g->parts_off = rfsn::align_up(g->calls_off + calls, 256);
-    g->bytes = rfsn::align_up(g->parts_off + parts, 256);
+    const size_t words = sizeof(uint2) * 2 * (size_t)rfsn::kMaxPeers * g->groups * rfsn::kPeerSlots * (g->head_dim + 2);
+    g->calls_off = 256;
+    g->words_off = rfsn::align_up(g->calls_off + calls, 256);
+    g->bytes = rfsn::align_up(g->words_off + words, 256);
 }
 
 }  // namespace
@@ -121,8 +120,7 @@ rfsn_status rfsn_paged_attention_peer(const rfsn_arena* arena, const float* q, i
     pp.rank = peers->rank;
     for (int r = 0; r < peers->world; ++r) {
         char* base = static_cast<char*>(peers->mapped[r]);
-        pp.parts[r] = reinterpret_cast<float*>(base + peers->parts_off);
-        pp.flags[r] = reinterpret_cast<int*>(base + peers->flags_off);
+        pp.words[r] = reinterpret_cast<uint2*>(base + peers->words_off);
     }
     pp.calls = reinterpret_cast<int*>(static_cast<char*>(peers->local) + peers->calls_off);
     pp.timeout_ns = peers->timeout_ns;
