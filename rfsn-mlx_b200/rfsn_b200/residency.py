@@ -11,11 +11,13 @@ decisions and metrics match bit for bit:
   block right before a warm block under the same condition;
 * completions are consumed on the caller's thread.
 
-What changes is the data path. The worker thread only reads and
-decompresses the cold payload into pinned host memory. When the caller
-drains it, the block is copied into the device arena with an asynchronous
-host-to-device copy on a side stream, and the compute stream waits on that
-copy's event, so the upload overlaps whatever the compute stream is doing.
+What changes is the data path. The worker thread reads, verifies and
+decompresses the cold payload (numpy, off the caller's thread). When the
+caller drains it, the payload is staged in pinned host memory and copied into
+the device arena with an asynchronous host-to-device copy on a side stream;
+the compute stream waits on that copy's event before its next kernel.
+One exact shortcut: a decode-step prefetch check on a layer without any cold
+block returns at once (both candidate rules need a cold block).
 """
 
 from __future__ import annotations
@@ -87,7 +89,11 @@ class ResidencyManager:
 
     def maybe_schedule_prefetch(self, cache: "LayerKVCache", query_abs_pos: int) -> None:
         self.drain_completed_prefetches(cache)
-        manifests = [m for m in cache.block_manager.iter_blocks(layer_id=cache.layer_id) if m.materializable]
+        live = cache.block_manager.page_table.layer_entries(cache.layer_id)
+        # Both candidate rules need a cold block; with none, nothing can be scheduled.
+        if not any(m.residency == BlockLocation.COLD_DISK for m in live):
+            return
+        manifests = [m for m in live if m.materializable]
         if len(manifests) < 2:
             return
         trigger = lambda m: query_abs_pos >= m.logical_end - self.prefetch_margin_tokens  # noqa: E731
