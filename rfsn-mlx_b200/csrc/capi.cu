@@ -114,6 +114,7 @@ void choose_splits(int total_tiles, int groups_x_qblocks, int target, int max_sp
 }
 
 constexpr int kFastStages = 3;
+constexpr int kPrefillMinRows = 64;  // query rows from which the tcgen05 prefill kernel is used
 constexpr int kFastCtasPerSm = 2;
 constexpr int kGenericMaxSplits = 256;
 
@@ -388,6 +389,38 @@ rfsn_status rfsn::paged_attention_impl(const rfsn_arena* arena, const float* q, 
     }
     const int sms = sm_count_cached();
     const bool use_fast = arena->has_tma && arena->head_dim == 128 && a.nslots <= 4;
+    // chunked prefill on the tensor cores: float4 q/out rows need 16-byte alignment
+    const bool use_prefill = peer == nullptr && arena->has_tma && arena->head_dim == 128 && q_len >= kPrefillMinRows &&
+                             a.G <= 128 && (uintptr_t)q % 16 == 0 && (uintptr_t)out % 16 == 0;
+    if (use_prefill) {
+        const WsLayout w = ws_layout(a.groups, 1, 1, a.slots_ws, 128);
+        if (w.total > workspace_bytes) {
+            set_error("attention workspace too small: need %zu bytes, have %zu", w.total, workspace_bytes);
+            return RFSN_ERR_OVERFLOW;
+        }
+        PrefillParams pp;
+        memset(&pp, 0, sizeof(pp));
+        pp.q = q;
+        pp.out = out;
+        pp.lse = lse;
+        pp.records = reinterpret_cast<const int4*>(table->records);
+        pp.n_blocks = table->n_blocks;
+        pp.ring_row0 = hot->ring_row0;
+        pp.capacity = hot->capacity;
+        pp.head = hot->head_index;
+        pp.hlen = hot->length;
+        pp.hstart = hot->start_pos;
+        pp.rows = arena->rows;
+        pp.batch = batch;
+        pp.q_heads = q_heads;
+        pp.kv_heads = kv_heads;
+        pp.q_len = q_len;
+        pp.q_pos0 = q_pos0;
+        pp.groups_per_kv = a.G;
+        pp.qscale = qscale_for(128);
+        pp.ws = ws_view(workspace, w);
+        return prefill_launch(arena->dtype, arena->maps, pp, s);
+    }
     if (peer != nullptr && !use_fast) {
         set_error("fused cross-GPU merge needs the tensor-core decode shape (bf16/f16, head_dim 128, <= 4 query "
                   "slots per KV head)");

@@ -36,6 +36,20 @@ struct Params {
 };
 }  // namespace fast
 
+// Chunked-prefill tensor-core kernel (prefill_attn.cu).
+struct PrefillParams {
+    const float* q;
+    float* out;
+    float* lse;
+    const int4* records;
+    int n_blocks;
+    int ring_row0, capacity, head, hlen, hstart;
+    int rows;                 // arena rows per head
+    int batch, q_heads, kv_heads, q_len, q_pos0, groups_per_kv;
+    float qscale;             // 1/sqrt(D) * log2(e)
+    WsView ws;                // error word only
+};
+
 namespace generic {
 struct Params {
     const float* q;
@@ -68,6 +82,8 @@ rfsn_status paged_attention_impl(const rfsn_arena* arena, const float* q, int ba
                                  int q_len, int q_pos0, const rfsn_page_table* table, const rfsn_hot_window* hot,
                                  float* out, float* lse, void* workspace, size_t workspace_bytes, int max_splits,
                                  const PeerParams* peer, cudaStream_t stream);
+// prefill_attn.cu
+rfsn_status prefill_launch(int dtype, const CUtensorMap* maps, const PrefillParams& p, cudaStream_t stream);
 // merge.cu
 rfsn_status lse_merge_launch(const float* parts_out, const float* parts_lse, int n_parts, int rows, int head_dim,
                              float* out, float* lse_out, cudaStream_t stream);

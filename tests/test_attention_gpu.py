@@ -169,3 +169,38 @@ def test_empty_context_is_rejected_like_reference():
     lay = make_layout("bfloat16", 1, 8, 128, [], 64, 0, 0, seed=14)
     with pytest.raises(ValueError, match="at least one KV segment"):
         run_paged(lay, _q(14, 1, 32, 1, 128), 0)
+
+
+# ----------------------------------------------------------------------------------------
+# chunked prefill on tcgen05 tensor cores (q_len >= 64, head_dim 128, bf16/fp16):
+# q and P enter the products as 16-bit high + residual parts, so the float32 guard holds.
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
+@pytest.mark.parametrize("q_len,G,blocks,ring,hot,head", [
+    (64, 4, [1000, 1000, 24], 4096, 600, 100),      # chunk at the end of the hot window
+    (128, 4, [256] * 6, 2048, 2048, 512),          # wrapped full ring
+    (200, 2, [1000, 333, 77], 512, 400, 300),      # ragged chunk, odd span lengths
+    (512, 4, [512] * 4, 1024, 1024, 0),            # many CTAs per KV head
+    (100, 3, [129, 7], 256, 250, 200),             # 3 query heads per KV head (42 positions per CTA)
+    (96, 8, [300], 128, 128, 64),                  # 8 query heads per KV head
+    (70, 1, [64, 64, 1], 64, 64, 0),               # no GQA; 8-row boxes only
+])
+def test_tensor_core_prefill_matches_oracle(dtype, q_len, G, blocks, ring, hot, head):
+    Hkv = 4
+    lay = make_layout(dtype, 1, Hkv, 128, blocks, ring, hot, head, seed=81)
+    q = _q(81, 1, Hkv * G, q_len, 128)
+    _check(lay, q, lay.total_tokens - q_len)
+
+
+def test_tensor_core_prefill_chunk_in_the_middle_of_history_batch2():
+    # queries that do not sit at the end: keys after each query position are masked
+    lay = make_layout("bfloat16", 2, 8, 128, [1000] * 3, 1024, 1000, 24, seed=82)
+    q = _q(82, 2, 32, 300, 128)
+    _check(lay, q, 1500)
+
+
+def test_tensor_core_prefill_peaky_scores():
+    # large, concentrated scores (attention-sink-like): a 16-bit q alone would be off by >1e-2
+    lay = make_layout("bfloat16", 1, 2, 128, [256, 256], 256, 200, 0, seed=83)
+    rng = np.random.default_rng(83)
+    q = (rng.standard_normal((1, 8, 128, 128)) * 6.0).astype(np.float32)
+    _check(lay, q, lay.total_tokens - 128)
