@@ -16,19 +16,25 @@
 // in 16 bits already, so they enter the products exactly.
 //
 // Warps:
-//   0-3  softmax (thread = row = TMEM lane): split q into shared memory
-//        (128B-swizzled K-major), then per key tile read the S row from TMEM,
-//        causal/validity mask, float32 online softmax on exp2, write Phi/Plo
-//        back over the S columns (A operand of the PV product, read from
-//        TMEM), rescale the O row in TMEM when its maximum grew; finally
-//        O / l -> out and the log-sum-exp.
-//   4    producer: walks the page table (archived blocks in order, then the
-//        hot pieces) in 128-key tiles up to the CTA's causal limit, streaming
-//        K/V with TMA into a 2-stage ring (8-row boxes for ragged span ends).
-//   5    MMA issuer (one thread): S(it+1) into the other S buffer while the
-//        softmax works on tile it, then O += P(it) V(it); tcgen05.commit
-//        signals the softmax warps and releases the K/V stage.
-// TMEM: S buffers at columns [0,128) and [128,256), O at [256,384).
+//   0-7  softmax: warp w owns TMEM lane quarter w % 4 (32 rows, thread = row)
+//        and key half w / 4 (64 of the 128 keys of a tile). They split q into
+//        TMEM (the A operand of S: shared memory bandwidth is left to the K/V
+//        operands and the TMA fills); per key tile they read their S
+//        half from TMEM, apply the causal/validity mask, exchange row maxima
+//        with the partner warp (mbarrier per quarter), run the float32 online
+//        softmax on exp2, write Phi/Plo back over the S columns (the A operand
+//        of the PV product, read from TMEM) and rescale their half of the O row
+//        when the reference maximum moves; finally O / l -> out and the
+//        log-sum-exp.
+//   8    K producer: walks the page table (archived blocks in order, then the
+//        hot pieces) in 128-key tiles up to the CTA's causal limit, posts each
+//        tile's {position, length} and streams K with TMA into a 3-stage ring
+//        (8-row boxes for ragged span ends).
+//   9    MMA issuer (one thread): S(t) = Q K(t)^T into S buffer t % 2, then
+//        O += P(t-1) V(t-1), both with A from TMEM; tcgen05.commit signals the
+//        softmax warps and releases K stages (after S) and V stages (after PV).
+//   10   V producer: the same walk, streaming V into a 3-stage ring.
+// TMEM: two S/P buffers at columns [0,256), O at [256,384), q hi/lo at [384,512).
 // Every mbarrier wait is bounded (error flag + early exit) and TMEM is
 // released on every path.
 #include <math_constants.h>
@@ -45,41 +51,60 @@ namespace prefill {
 constexpr int D = 128;
 constexpr int BM = 128;   // rows per CTA (positions x query heads of one KV head)
 constexpr int BN = 128;   // keys per tile
-constexpr int NST = 2;    // K/V pipeline stages
-constexpr int NTHREADS = 6 * 32;
+constexpr int KST = 3;    // K ring stages (released after S)
+constexpr int VST = 3;    // V ring stages (released after PV)
+constexpr int NSB = 2;    // S/P buffers in TMEM
+// Tile-info ring: slot t % NINFO is rewritten for tile t + NINFO after K stage
+// reuse (S(t + NINFO - KST) done), which needs PV(t + NINFO - KST - NSB) done,
+// i.e. the softmax of tile t finished when NINFO >= KST + NSB.
+constexpr int NINFO = 8;
+static_assert(NINFO >= KST + NSB, "tile-info ring too short");
+constexpr int SOFTMAX_WARPS = 8;  // two warps per 32-row TMEM quarter, one per 64-key half
+constexpr int KPROD_WARP = SOFTMAX_WARPS, MMA_WARP = SOFTMAX_WARPS + 1, VPROD_WARP = SOFTMAX_WARPS + 2;
+constexpr int NTHREADS = (SOFTMAX_WARPS + 3) * 32;
+constexpr int SOFTMAX_THREADS = SOFTMAX_WARPS * 32;
 constexpr int TILE_HALF = BN * 128;  // bytes of one 64-column half of a 128-row tile
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t COL_S0 = 0, COL_S1 = 128, COL_O = 256;
+constexpr uint32_t COL_O = 256;                  // float32 O accumulator, 128 columns
+constexpr uint32_t COL_QHI = 384, COL_QLO = 448;  // q as the A operand of S: 16-bit pairs, 64 columns each
 
 struct Smem {
-    uint8_t q[2][2][BM * 128];  // [hi/lo][column half]
-    uint8_t k[NST][2][TILE_HALF];
-    uint8_t v[NST][2][TILE_HALF];
-    uint64_t kv_full[NST];
-    uint64_t kv_empty[NST];
-    uint64_t s_full[2];
-    uint64_t p_full;
-    uint64_t o_done;
+    uint8_t k[KST][2][TILE_HALF];
+    uint8_t v[VST][2][TILE_HALF];
+    uint64_t k_full[KST], k_empty[KST];  // K stage loaded / free again (after S)
+    uint64_t v_full[VST], v_empty[VST];  // V stage loaded / free again (after PV)
+    uint64_t info_full[NINFO];           // tile info posted (count 1)
+    uint64_t s_full[NSB];                // S(t) in TMEM buffer t % NSB
+    uint64_t p_full[NSB];                // P(t) written over it (count: softmax threads)
+    uint64_t o_done;                     // PV(t) complete, one phase per tile
+    uint64_t pv_done[NSB];               // PV(t) complete, per S/P buffer t % NSB
     uint64_t mma_done;
-    int2 tinfo[NST];  // {kpos0, nvalid}; nvalid < 0 marks the end of the key stream
+    uint64_t pair[4][2];  // per 32-row quarter and tile parity: both key halves posted their maxima
+    uint64_t pair_l[4];   // per quarter: both halves posted their partial sums (end of the stream)
+    float red[2][2][BM];  // [tile parity][key half][row] partial maxima; [0][*] reused for sums
+    int2 tinfo[NINFO];    // {kpos0, nvalid} per tile (ring); nvalid < 0 marks the end of the key stream
     uint32_t tmem;
     int abort;
 };
 
-// (a, b) -> packed 16-bit high parts and packed 16-bit residuals.
+// (a, b) -> packed 16-bit high parts and packed 16-bit residuals (a = hi + lo to
+// ~16 significand bits). bf16: rounding by integer add on the bit pattern (half
+// away from zero on the magnitude; the inputs are finite) and a byte permute,
+// which keeps the conversions off the special-function pipe that runs exp2.
 template <typename T>
 __device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
-    hi = pack2<T>(a, b);
-    float ha, hb;
     if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-        ha = __uint_as_float(hi << 16);
-        hb = __uint_as_float(hi & 0xffff0000u);
+        const uint32_t ha = (__float_as_uint(a) + 0x8000u) & 0xffff0000u;
+        const uint32_t hb = (__float_as_uint(b) + 0x8000u) & 0xffff0000u;
+        const uint32_t la = __float_as_uint(a - __uint_as_float(ha)) + 0x8000u;
+        const uint32_t lb = __float_as_uint(b - __uint_as_float(hb)) + 0x8000u;
+        hi = __byte_perm(ha, hb, 0x7632);
+        lo = __byte_perm(la, lb, 0x7632);
     } else {
+        hi = pack2<T>(a, b);
         const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hi));
-        ha = f.x;
-        hb = f.y;
+        lo = pack2<T>(a - f.x, b - f.y);
     }
-    lo = pack2<T>(a - ha, b - hb);
 }
 
 // Bounded wait whose result is the same on every lane of the warp, so the
@@ -93,13 +118,81 @@ __device__ __forceinline__ void fail(int* abort_flag, const PrefillParams& p) {
     atomicExch(p.ws.error, kDevErrTimeout);
 }
 
+// The CTA's key stream: archived blocks in table order, then the hot window's
+// two ring pieces, cut into tiles of at most BN keys, up to the causal limit.
+struct TileWalk {
+    int span = 0, off = 0;
+    int s_row = 0, s_pos = 0, s_len = 0;
+
+    __device__ __forceinline__ bool load_span(const PrefillParams& p) {
+        while (span < p.n_blocks + 2) {
+            if (span < p.n_blocks) {
+                const int4 r = p.records[span];
+                s_row = r.x;
+                s_pos = r.y;
+                s_len = r.z;
+            } else {
+                const int first = min(p.hlen, p.capacity - p.head);
+                if (span == p.n_blocks) {
+                    s_row = p.ring_row0 + p.head;
+                    s_pos = p.hstart;
+                    s_len = first;
+                } else {
+                    s_row = p.ring_row0;
+                    s_pos = p.hstart + first;
+                    s_len = p.hlen - first;
+                }
+            }
+            if (s_len > 0) return true;
+            ++span;
+        }
+        return false;
+    }
+    // Next tile: key positions [kpos0, kpos0 + nvalid) at arena row `row`.
+    __device__ __forceinline__ bool next(const PrefillParams& p, int qlast, int& kpos0, int& row, int& nvalid) {
+        if (off == 0 && !load_span(p)) return false;
+        kpos0 = s_pos + off;
+        if (kpos0 > qlast) return false;  // spans are in increasing position order
+        row = s_row + off;
+        nvalid = min(BN, s_len - off);
+        off += BN;
+        if (off >= s_len) {
+            off = 0;
+            ++span;
+        }
+        return true;
+    }
+};
+
+// One K or V tile -> a stage (two 64-column halves): 64-row boxes for a full
+// tile, 8-row boxes for a ragged span end.
+__device__ __forceinline__ void load_tile(uint8_t (*dst)[TILE_HALF], const CUtensorMap* m64, const CUtensorMap* m8,
+                                          int grow, int nvalid, uint64_t* bar) {
+    if (nvalid == BN) {
+        mbar_arrive_expect_tx(bar, 2 * TILE_HALF);
+        for (int hh = 0; hh < 2; ++hh)
+            for (int r64 = 0; r64 < 2; ++r64) tma_load_2d(dst[hh] + r64 * 64 * 128, m64, 64 * hh, grow + 64 * r64, bar);
+    } else {
+        const int nb = (nvalid + 7) >> 3;
+        mbar_arrive_expect_tx(bar, nb * 2 * 1024);
+        for (int hh = 0; hh < 2; ++hh)
+            for (int bb = 0; bb < nb; ++bb) tma_load_2d(dst[hh] + bb * 1024, m8, 64 * hh, grow + 8 * bb, bar);
+    }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(NTHREADS, 1)
 prefill_attn_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_constant__ CUtensorMap mapV64,
                     const __grid_constant__ CUtensorMap mapK8, const __grid_constant__ CUtensorMap mapV8,
                     const PrefillParams p) {
-    extern __shared__ uint8_t smem_raw[];
-    Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // The swizzled operand tiles need 1024-byte alignment; the dynamic window
+    // starts aligned when the kernel has no static shared memory (checked).
+    if ((smem_u32(smem_raw) & 1023u) != 0) {
+        if (threadIdx.x == 0) atomicExch(p.ws.error, kDevErrBadTable);
+        return;
+    }
+    Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = p.groups_per_kv;
     const int ppc = BM / G;                                   // chunk positions per CTA
@@ -111,23 +204,35 @@ prefill_attn_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
 
     // ---- set-up: zero the K/V stages (rows past a ragged span end stay finite),
     //      barriers, TMEM ----
-    for (int i = tid; i < NST * 2 * 2 * TILE_HALF / 16; i += NTHREADS) {
+    for (int i = tid; i < (KST + VST) * 2 * TILE_HALF / 16; i += NTHREADS) {
         reinterpret_cast<uint4*>(sm.k)[i] = make_uint4(0, 0, 0, 0);
     }
     if (tid == 0) {
-        for (int s = 0; s < NST; ++s) {
-            mbar_init(&sm.kv_full[s], 1);
-            mbar_init(&sm.kv_empty[s], 1);
+        for (int s = 0; s < KST; ++s) {
+            mbar_init(&sm.k_full[s], 1);
+            mbar_init(&sm.k_empty[s], 1);
         }
-        mbar_init(&sm.s_full[0], 1);
-        mbar_init(&sm.s_full[1], 1);
-        mbar_init(&sm.p_full, 4 * 32);
+        for (int s = 0; s < VST; ++s) {
+            mbar_init(&sm.v_full[s], 1);
+            mbar_init(&sm.v_empty[s], 1);
+        }
+        for (int i = 0; i < NINFO; ++i) mbar_init(&sm.info_full[i], 1);
+        for (int i = 0; i < NSB; ++i) {
+            mbar_init(&sm.s_full[i], 1);
+            mbar_init(&sm.p_full[i], SOFTMAX_THREADS);
+            mbar_init(&sm.pv_done[i], 1);
+        }
         mbar_init(&sm.o_done, 1);
         mbar_init(&sm.mma_done, 1);
+        for (int qd = 0; qd < 4; ++qd) {
+            mbar_init(&sm.pair[qd][0], 64);
+            mbar_init(&sm.pair[qd][1], 64);
+            mbar_init(&sm.pair_l[qd], 64);
+        }
         sm.abort = 0;
         fence_mbar_init();
     }
-    if (warp == 5) {
+    if (warp == MMA_WARP) {
         tc::tmem_alloc(&sm.tmem, TMEM_COLS);
         tc::tmem_relinquish();
     }
@@ -137,153 +242,134 @@ prefill_attn_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
     tc::fence_after_sync();
     const uint32_t tmem = sm.tmem;
 
-    if (warp == 4) {
-        // ---------------- producer ----------------
+    if (warp == KPROD_WARP) {
+        // ---------------- K producer (+ tile info) ----------------
         if (lane == 0) {
             prefetch_tmap(&mapK64);
-            prefetch_tmap(&mapV64);
-            int it = 0;
-            bool stop = false;
-            for (int span = 0; span < p.n_blocks + 2 && !stop; ++span) {
-                int s_row, s_pos, s_len;
-                if (span < p.n_blocks) {
-                    const int4 r = p.records[span];
-                    s_row = r.x;
-                    s_pos = r.y;
-                    s_len = r.z;
+            prefetch_tmap(&mapK8);
+            TileWalk walk;
+            int it = 0, kpos0, row, nvalid;
+            while (walk.next(p, qlast, kpos0, row, nvalid)) {
+                const int s = it % KST;
+                // stage free once S(it - KST) is done
+                if (it >= KST && !mbar_wait_bounded(&sm.k_empty[s], ((it / KST) + 1) & 1, &sm.abort)) {
+                    fail(&sm.abort, p);
+                    break;
+                }
+                const bool bad = row < 0 || row + nvalid > p.rows;
+                if (bad) atomicExch(p.ws.error, kDevErrBadTable);
+                sm.tinfo[it % NINFO] = make_int2(kpos0, bad ? 0 : nvalid);
+                mbar_arrive(&sm.info_full[it % NINFO]);
+                if (bad) {
+                    mbar_arrive(&sm.k_full[s]);
                 } else {
-                    const int first = min(p.hlen, p.capacity - p.head);
-                    if (span == p.n_blocks) {
-                        s_row = p.ring_row0 + p.head;
-                        s_pos = p.hstart;
-                        s_len = first;
-                    } else {
-                        s_row = p.ring_row0;
-                        s_pos = p.hstart + first;
-                        s_len = p.hlen - first;
-                    }
+                    load_tile(sm.k[s], &mapK64, &mapK8, bh * p.rows + row, nvalid, &sm.k_full[s]);
                 }
-                for (int off = 0; off < s_len; off += BN) {
-                    const int kpos0 = s_pos + off;
-                    if (kpos0 > qlast) {  // spans are in increasing position order
-                        stop = true;
-                        break;
-                    }
-                    const int nvalid = min(BN, s_len - off);
-                    const int row = s_row + off;
-                    const int s = it % NST;
-                    if (it >= NST && !mbar_wait_bounded(&sm.kv_empty[s], ((it / NST) + 1) & 1, &sm.abort)) {
-                        fail(&sm.abort, p);
-                        stop = true;
-                        break;
-                    }
-                    const bool bad = row < 0 || row + nvalid > p.rows;
-                    if (bad) atomicExch(p.ws.error, kDevErrBadTable);
-                    sm.tinfo[s] = make_int2(kpos0, bad ? 0 : nvalid);
-                    const int grow = bh * p.rows + row;
-                    if (bad) {
-                        mbar_arrive(&sm.kv_full[s]);
-                    } else if (nvalid == BN) {
-                        mbar_arrive_expect_tx(&sm.kv_full[s], 4 * TILE_HALF);
-                        for (int hh = 0; hh < 2; ++hh) {
-                            for (int r64 = 0; r64 < 2; ++r64) {
-                                tma_load_2d(sm.k[s][hh] + r64 * 64 * 128, &mapK64, 64 * hh, grow + 64 * r64, &sm.kv_full[s]);
-                                tma_load_2d(sm.v[s][hh] + r64 * 64 * 128, &mapV64, 64 * hh, grow + 64 * r64, &sm.kv_full[s]);
-                            }
-                        }
-                    } else {
-                        const int nb = (nvalid + 7) >> 3;
-                        mbar_arrive_expect_tx(&sm.kv_full[s], nb * 4 * 1024);
-                        for (int hh = 0; hh < 2; ++hh) {
-                            for (int bb = 0; bb < nb; ++bb) {
-                                tma_load_2d(sm.k[s][hh] + bb * 1024, &mapK8, 64 * hh, grow + 8 * bb, &sm.kv_full[s]);
-                                tma_load_2d(sm.v[s][hh] + bb * 1024, &mapV8, 64 * hh, grow + 8 * bb, &sm.kv_full[s]);
-                            }
-                        }
-                    }
-                    ++it;
-                }
+                ++it;
             }
-            // let the fills in flight land (bounded) before the marker reuses a stage
-            for (int j = max(0, it - NST); j < it; ++j) mbar_wait_bounded(&sm.kv_full[j % NST], (j / NST) & 1, nullptr);
-            // end-of-stream marker
-            const int s = it % NST;
-            if (it < NST || mbar_wait_bounded(&sm.kv_empty[s], ((it / NST) + 1) & 1, &sm.abort)) {
-                sm.tinfo[s] = make_int2(0, -1);
-                mbar_arrive(&sm.kv_full[s]);
+            // K fills in flight land first (bounded): the marker below reuses a K barrier
+            for (int j = max(0, it - KST); j < it; ++j) mbar_wait_bounded(&sm.k_full[j % KST], (j / KST) & 1, nullptr);
+            // end-of-stream marker: tile info for the softmax warps, a K "fill" for the MMA issuer
+            const int s = it % KST;
+            if (!sm.abort && (it < KST || mbar_wait_bounded(&sm.k_empty[s], ((it / KST) + 1) & 1, &sm.abort))) {
+                sm.tinfo[it % NINFO] = make_int2(0, -1);
+                mbar_arrive(&sm.info_full[it % NINFO]);
+                mbar_arrive(&sm.k_full[s]);
             } else {
                 fail(&sm.abort, p);
             }
         }
-    } else if (warp == 5) {
+    } else if (warp == VPROD_WARP) {
+        // ---------------- V producer ----------------
+        if (lane == 0) {
+            prefetch_tmap(&mapV64);
+            prefetch_tmap(&mapV8);
+            TileWalk walk;
+            int it = 0, kpos0, row, nvalid;
+            while (walk.next(p, qlast, kpos0, row, nvalid)) {
+                const int s = it % VST;
+                // stage free once PV(it - VST) is done
+                if (it >= VST && !mbar_wait_bounded(&sm.v_empty[s], ((it / VST) + 1) & 1, &sm.abort)) {
+                    fail(&sm.abort, p);
+                    break;
+                }
+                if (row < 0 || row + nvalid > p.rows) {
+                    mbar_arrive(&sm.v_full[s]);
+                } else {
+                    load_tile(sm.v[s], &mapV64, &mapV8, bh * p.rows + row, nvalid, &sm.v_full[s]);
+                }
+                ++it;
+            }
+            // V fills in flight land before the CTA can exit
+            for (int j = max(0, it - VST); j < it; ++j) mbar_wait_bounded(&sm.v_full[j % VST], (j / VST) & 1, nullptr);
+        }
+    } else if (warp == MMA_WARP) {
         // ---------------- MMA issuer ----------------
-        named_barrier_sync(2, 5 * 32);  // q tiles written by the softmax warps
+        named_barrier_sync(1, SOFTMAX_THREADS + 32);  // q written into TMEM by the softmax warps
         tc::fence_after_sync();
         if (lane == 0) {
             constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
             const uint32_t id_qk = tc::idesc_f16(kBf16, false, false, BM, BN);
             const uint32_t id_pv = tc::idesc_f16(kBf16, false, true, BM, D);
             const uint32_t tO = tmem + COL_O;
-            int it = 0;
             bool pending = false;  // tensor-core work issued whose completion is not yet observed
-            bool have_first = mbar_wait_bounded(&sm.kv_full[0], 0, &sm.abort);
-            if (!have_first) fail(&sm.abort, p);
-            have_first = have_first && sm.tinfo[0].y >= 0;
-            for (int t = 0; have_first; ++t) {
-                // S(t) = Qhi K^T + Qlo K^T into S buffer t % 2; t = 0 first, then S(it+1)
-                // one tile ahead while the softmax works on tile it
-                if (t > 0) {
-                    it = t - 1;
-                    const int s1 = t % NST;
-                    if (!mbar_wait_bounded(&sm.kv_full[s1], (t / NST) & 1, &sm.abort)) {
-                        fail(&sm.abort, p);
-                        break;
-                    }
+            // t: tile whose S is issued this round; it = t - 1: tile whose PV follows
+            for (int t = 0;; ++t) {
+                const int it = t - 1;
+                const int ks = t % KST;
+                if (!mbar_wait_bounded(&sm.k_full[ks], (t / KST) & 1, &sm.abort)) {
+                    fail(&sm.abort, p);
+                    break;
                 }
-                const bool issue = (t == 0) || sm.tinfo[t % NST].y >= 0;
+                const bool issue = sm.tinfo[t % NINFO].y >= 0;
                 if (issue) {
-                    // S buffer t % 2 last held P(t-2): PV(t-2) must be done
-                    if (t >= 2 && !mbar_wait_bounded(&sm.o_done, (t - 2) & 1, &sm.abort)) {
+                    // S buffer t % NSB last held P(t - NSB): PV(t - NSB) must be done. A
+                    // per-buffer barrier: o_done may already be two phases past t - NSB,
+                    // which a parity wait could not tell from the phase itself.
+                    if (t >= NSB && !mbar_wait_bounded(&sm.pv_done[t % NSB], ((t / NSB) + 1) & 1, &sm.abort)) {
                         fail(&sm.abort, p);
                         break;
                     }
                     tc::fence_after_sync();
-                    const int s = t % NST;
-                    const uint32_t tS = tmem + ((t & 1) ? COL_S1 : COL_S0);
+                    // S(t) = Qhi K^T + Qlo K^T
+                    const uint32_t tS = tmem + 128 * (t % NSB);
+#pragma unroll 1
+                    for (int part = 0; part < 2; ++part) {
+                        const uint32_t tQ = tmem + (part ? COL_QLO : COL_QHI);
+#pragma unroll
+                        for (int kk = 0; kk < 8; ++kk) {
+                            const uint32_t ka = smem_u32(sm.k[ks][kk >> 2]) + (kk & 3) * 32;
+                            tc::mma_f16_ts(tS, tQ + 8 * kk, tc::smem_desc_sw128(ka, 16, 1024), id_qk, part > 0 || kk > 0);
+                        }
+                    }
+                    tc::commit(&sm.s_full[t % NSB]);
+                    tc::commit(&sm.k_empty[ks]);
+                    pending = true;
+                }
+                if (it >= 0) {
+                    // P(it) in TMEM (and O rescaled): O += Phi V + Plo V
+                    const int vs = it % VST;
+                    if (!mbar_wait_bounded(&sm.p_full[it % NSB], (it / NSB) & 1, &sm.abort) ||
+                        !mbar_wait_bounded(&sm.v_full[vs], (it / VST) & 1, &sm.abort)) {
+                        fail(&sm.abort, p);
+                        break;
+                    }
+                    tc::fence_after_sync();
+                    const uint32_t tP = tmem + 128 * (it % NSB);
 #pragma unroll 1
                     for (int part = 0; part < 2; ++part) {
 #pragma unroll
                         for (int kk = 0; kk < 8; ++kk) {
-                            const uint32_t qa = smem_u32(sm.q[part][kk >> 2]) + (kk & 3) * 32;
-                            const uint32_t ka = smem_u32(sm.k[s][kk >> 2]) + (kk & 3) * 32;
-                            tc::mma_f16_ss(tS, tc::smem_desc_sw128(qa, 16, 1024), tc::smem_desc_sw128(ka, 16, 1024),
-                                           id_qk, part > 0 || kk > 0);
+                            const uint32_t va = smem_u32(sm.v[vs][0]) + kk * 16 * 128;
+                            tc::mma_f16_ts(tO, tP + 64 * part + 8 * kk, tc::smem_desc_sw128(va, TILE_HALF, 1024),
+                                           id_pv, it > 0 || part > 0 || kk > 0);
                         }
                     }
-                    tc::commit(&sm.s_full[t & 1]);
-                    pending = true;
+                    tc::commit(&sm.o_done);
+                    tc::commit(&sm.pv_done[it % NSB]);
+                    tc::commit(&sm.v_empty[vs]);
                 }
-                if (t == 0) continue;
-                // P(it) in TMEM (and O rescaled): O += Phi V + Plo V
-                if (!mbar_wait_bounded(&sm.p_full, it & 1, &sm.abort)) {
-                    fail(&sm.abort, p);
-                    break;
-                }
-                tc::fence_after_sync();
-                const int s = it % NST;
-                const uint32_t tP = tmem + ((it & 1) ? COL_S1 : COL_S0);
-#pragma unroll 1
-                for (int part = 0; part < 2; ++part) {
-#pragma unroll
-                    for (int kk = 0; kk < 8; ++kk) {
-                        const uint32_t va = smem_u32(sm.v[s][0]) + kk * 16 * 128;
-                        tc::mma_f16_ts(tO, tP + 64 * part + 8 * kk, tc::smem_desc_sw128(va, TILE_HALF, 1024), id_pv,
-                                       it > 0 || part > 0 || kk > 0);
-                    }
-                }
-                tc::commit(&sm.o_done);
-                tc::commit(&sm.kv_empty[s]);
-                if (!issue) break;  // tile it was the last one
+                if (!issue) break;  // end of the key stream
             }
             // drain: no tensor-core work may be in flight when TMEM is released
             // (tcgen05.commit tracks all earlier tensor-core work of this thread)
@@ -293,117 +379,140 @@ prefill_attn_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
             }
         }
     } else {
-        // ---------------- softmax warps (thread = row = TMEM lane) ----------------
-        const int r = tid;
+        // ---------------- softmax warps ----------------
+        // warp w: TMEM lane quarter qd = w % 4 (rows 32 qd + lane), key half ch = w / 4
+        const int qd = warp & 3, ch = warp >> 2;
+        {
+            // q row -> TMEM (A operand layout: row = lane, dims packed in pairs along the
+            // columns). Warp w stages dims [64 (w / 4), +64) of the rows of its quarter.
+            const int r = 32 * qd + lane;
+            const int g = r % G, j = r / G;
+            const int qrow = pos_base + j;
+            const bool ok_row = j < ppc && qrow < p.q_len;
+            const float* src = p.q + (((size_t)b * p.q_heads + hk * G + g) * p.q_len + (ok_row ? qrow : 0)) * D + 64 * ch;
+            uint32_t hi[32], lo[32];
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {  // 16 chunks of 4 elements
+                float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (ok_row) a = *reinterpret_cast<const float4*>(src + 4 * c);
+                split2<T>(a.x * p.qscale, a.y * p.qscale, hi[2 * c], lo[2 * c]);
+                split2<T>(a.z * p.qscale, a.w * p.qscale, hi[2 * c + 1], lo[2 * c + 1]);
+            }
+            const uint32_t lane_q = (uint32_t)(32 * qd) << 16;
+            tc::st_32x32b_x32(tmem + lane_q + COL_QHI + 32 * ch, hi);
+            tc::st_32x32b_x32(tmem + lane_q + COL_QLO + 32 * ch, lo);
+            tc::wait_st();
+        }
+        tc::fence_before_sync();
+        named_barrier_sync(1, SOFTMAX_THREADS + 32);
+
+        const int r = 32 * qd + lane;  // this thread's row = TMEM lane
         const int g = r % G, j = r / G;
         const int h = hk * G + g;
         const int qrow = pos_base + j;
         const bool row_ok = j < ppc && qrow < p.q_len;
         const int qpos = p.q_pos0 + qrow;
-        {
-            const float* src = p.q + (((size_t)b * p.q_heads + h) * p.q_len + (row_ok ? qrow : 0)) * D;
-#pragma unroll
-            for (int c = 0; c < 16; ++c) {  // 16 chunks of 8 elements
-                float x[8];
-                if (row_ok) {
-                    const float4 a = *reinterpret_cast<const float4*>(src + 8 * c);
-                    const float4 bq = *reinterpret_cast<const float4*>(src + 8 * c + 4);
-                    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
-                    x[4] = bq.x; x[5] = bq.y; x[6] = bq.z; x[7] = bq.w;
-                } else {
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) x[e] = 0.f;
-                }
-                uint32_t hi[4], lo[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) split2<T>(x[2 * e] * p.qscale, x[2 * e + 1] * p.qscale, hi[e], lo[e]);
-                const uint32_t off = tc::sw128_offset(r, c & 7);
-                *reinterpret_cast<uint4*>(sm.q[0][c >> 3] + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                *reinterpret_cast<uint4*>(sm.q[1][c >> 3] + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-            }
-        }
-        tc::fence_proxy_async_smem();
-        tc::fence_before_sync();
-        named_barrier_sync(2, 5 * 32);
-        const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
-        const uint32_t tO = tmem + COL_O + lane_base;
+        const uint32_t lane_base = (uint32_t)(32 * qd) << 16;
+        const uint32_t tO = tmem + COL_O + lane_base + 64 * ch;
         float m = -CUDART_INF_F, l = 0.f;
+        bool failed = false;
         int it = 0;
         for (;; ++it) {
-            const int s = it % NST;
-            if (!warp_wait(&sm.kv_full[s], (it / NST) & 1, &sm.abort)) break;
-            const int2 ti = sm.tinfo[s];
+            if (!warp_wait(&sm.info_full[it % NINFO], (it / NINFO) & 1, &sm.abort)) { failed = true; break; }
+            const int2 ti = sm.tinfo[it % NINFO];
             if (ti.y < 0) break;
-            if (!warp_wait(&sm.s_full[it & 1], (it >> 1) & 1, &sm.abort)) break;
+            if (!warp_wait(&sm.s_full[it % NSB], (it / NSB) & 1, &sm.abort)) { failed = true; break; }
             tc::fence_after_sync();
-            const uint32_t tS = tmem + ((it & 1) ? COL_S1 : COL_S0) + lane_base;
-            float sv[BN];
-#pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
-                uint32_t rr[32];
-                tc::ld_32x32b_x32(tS + 32 * cc, rr);
-                tc::wait_ld();
-#pragma unroll
-                for (int jj = 0; jj < 32; ++jj) sv[32 * cc + jj] = __uint_as_float(rr[jj]);
-            }
+            const uint32_t tS = tmem + 128 * (it % NSB) + lane_base;
+            uint32_t sr[64];
+            tc::ld_32x32b_x64_sync(tS + 64 * ch, sr);
             // keys [kpos0, kpos0 + nvalid) are valid; causal: key position <= query position
-            const int lim = min(ti.y, qpos - ti.x + 1);
-            float tmax = -CUDART_INF_F;
+            const int lim = min(ti.y, qpos - ti.x + 1) - 64 * ch;
+            float mx[4] = {-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F};
+            if (__all_sync(0xffffffffu, lim >= 64)) {
 #pragma unroll
-            for (int c = 0; c < BN; ++c) {
-                sv[c] = c < lim ? sv[c] : -CUDART_INF_F;
-                tmax = fmaxf(tmax, sv[c]);
-            }
-            const float mn = fmaxf(m, tmax);
-            const float alpha = (mn == -CUDART_INF_F) ? 1.f : exp2f(m - mn);
-            const float ms = (mn == -CUDART_INF_F) ? 0.f : mn;
-            float rs = 0.f;
+                for (int c = 0; c < 64; ++c) mx[c & 3] = fmaxf(mx[c & 3], __uint_as_float(sr[c]));
+            } else {
 #pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
-                uint32_t hi[16], lo[16];
-#pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    const float p0 = exp2f(sv[32 * cc + 2 * e] - ms);
-                    const float p1 = exp2f(sv[32 * cc + 2 * e + 1] - ms);
-                    rs += p0 + p1;
-                    split2<T>(p0, p1, hi[e], lo[e]);
+                for (int c = 0; c < 64; ++c) {
+                    const float x = c < lim ? __uint_as_float(sr[c]) : -CUDART_INF_F;
+                    sr[c] = __float_as_uint(x);
+                    mx[c & 3] = fmaxf(mx[c & 3], x);
                 }
-                tc::st_32x32b_x16(tS + 16 * cc, hi);
-                tc::st_32x32b_x16(tS + 64 + 16 * cc, lo);
             }
-            l = l * alpha + rs;
-            m = mn;
-            if (it > 0) {
-                // PV of the previous tile must be done before O is rescaled (and before
-                // this tile's P is published: one p_full phase per tile)
-                if (!warp_wait(&sm.o_done, (it - 1) & 1, &sm.abort)) break;
+            float tmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+            // row maximum over both key halves
+            sm.red[it & 1][ch][r] = tmax;
+            mbar_arrive(&sm.pair[qd][it & 1]);
+            if (!warp_wait(&sm.pair[qd][it & 1], (it >> 1) & 1, &sm.abort)) { failed = true; break; }
+            tmax = fmaxf(tmax, sm.red[it & 1][ch ^ 1][r]);
+            // Lazy rescaling: probabilities are taken relative to a reference maximum m
+            // that moves only when the row maximum exceeds it by more than 2^8 (or on the
+            // first tile). O and l share the reference, so O / l and the log-sum-exp are
+            // unchanged; p <= 256 keeps every term far from float32/bf16 overflow. Both
+            // warps of a row see the same values and take the same decision.
+            const float mn = fmaxf(m, tmax);
+            bool rescale = false;
+            if (it == 0) {
+                m = mn;
+            } else {
+                rescale = __any_sync(0xffffffffu, mn > m + 8.f);
+            }
+            float alpha = 1.f;
+            if (rescale && mn != m) {
+                alpha = (m == -CUDART_INF_F) ? 0.f : tc::ex2(m - mn);
+                m = mn;
+            }
+            const float ms = (m == -CUDART_INF_F) ? 0.f : m;
+            float rs[4] = {0.f, 0.f, 0.f, 0.f};
+            uint32_t hi[32], lo[32];
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+                const float p0 = tc::ex2(__uint_as_float(sr[2 * e]) - ms);
+                const float p1 = tc::ex2(__uint_as_float(sr[2 * e + 1]) - ms);
+                rs[e & 3] += p0 + p1;
+                split2<T>(p0, p1, hi[e], lo[e]);
+            }
+            // P columns: key k of the tile -> 16-bit element k (column k / 2); lo after hi
+            tc::st_32x32b_x32(tS + 32 * ch, hi);
+            tc::st_32x32b_x32(tS + 64 + 32 * ch, lo);
+            l = l * alpha + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
+            if (rescale) {
+                // PV of the previous tile must be done before O is rescaled
+                if (!warp_wait(&sm.o_done, (it - 1) & 1, &sm.abort)) { failed = true; break; }
                 tc::fence_after_sync();
-                if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll 1
+                for (int cc = 0; cc < 2; ++cc) {
+                    uint32_t rr[32];
+                    tc::ld_32x32b_x32_sync(tO + 32 * cc, rr);
 #pragma unroll
-                    for (int cc = 0; cc < 4; ++cc) {
-                        uint32_t rr[32];
-                        tc::ld_32x32b_x32(tO + 32 * cc, rr);
-                        tc::wait_ld();
-#pragma unroll
-                        for (int jj = 0; jj < 32; ++jj) rr[jj] = __float_as_uint(__uint_as_float(rr[jj]) * alpha);
-                        tc::st_32x32b_x32(tO + 32 * cc, rr);
-                    }
+                    for (int jj = 0; jj < 32; ++jj) rr[jj] = __float_as_uint(__uint_as_float(rr[jj]) * alpha);
+                    tc::st_32x32b_x32(tO + 32 * cc, rr);
                 }
             }
             tc::wait_st();
             tc::fence_before_sync();
-            mbar_arrive(&sm.p_full);
+            mbar_arrive(&sm.p_full[it % NSB]);
         }
-        const bool ok = it > 0 && warp_wait(&sm.o_done, (it - 1) & 1, &sm.abort) &&
-                        __all_sync(0xffffffffu, sm.abort == 0);
+        if (failed) fail(&sm.abort, p);
+        // row sum over both key halves. Once the last PV is done the partner has
+        // read every maximum posted here (it read them before publishing its P), so
+        // red[0] is free for the partial sums.
+        bool ok = !failed && it > 0 && warp_wait(&sm.o_done, (it - 1) & 1, &sm.abort);
+        if (ok) {
+            sm.red[0][ch][r] = l;
+            mbar_arrive(&sm.pair_l[qd]);
+            ok = warp_wait(&sm.pair_l[qd], 0, &sm.abort);
+        }
+        ok = ok && __all_sync(0xffffffffu, sm.abort == 0);
         tc::fence_after_sync();
-        float* dst = p.out + (((size_t)b * p.q_heads + h) * p.q_len + (row_ok ? qrow : 0)) * D;
-        const float inv = (ok && l > 0.f) ? 1.f / l : 0.f;
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
+        const float lt = ok ? l + sm.red[0][ch ^ 1][r] : 0.f;
+        float* dst = p.out + (((size_t)b * p.q_heads + h) * p.q_len + (row_ok ? qrow : 0)) * D + 64 * ch;
+        const float inv = (ok && lt > 0.f) ? 1.f / lt : 0.f;
+#pragma unroll 1
+        for (int cc = 0; cc < 2; ++cc) {
             uint32_t rr[32];
-            tc::ld_32x32b_x32(tO + 32 * cc, rr);
-            tc::wait_ld();
+            tc::ld_32x32b_x32_sync(tO + 32 * cc, rr);
             if (row_ok) {
 #pragma unroll
                 for (int jj = 0; jj < 32; jj += 4) {
@@ -414,15 +523,15 @@ prefill_attn_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
                 }
             }
         }
-        if (row_ok && p.lse != nullptr) {
+        if (row_ok && ch == 0 && p.lse != nullptr) {
             p.lse[((size_t)b * p.q_heads + h) * p.q_len + qrow] =
-                (ok && l > 0.f) ? (m + log2f(l)) * 0.69314718055994531f : -CUDART_INF_F;
+                (ok && lt > 0.f) ? (m + log2f(lt)) * 0.69314718055994531f : -CUDART_INF_F;
         }
         if (!ok && tid == 0 && it > 0) atomicExch(p.ws.error, kDevErrTimeout);
     }
     tc::fence_before_sync();
     __syncthreads();
-    if (warp == 5) {
+    if (warp == MMA_WARP) {
         __syncwarp();
         tc::fence_after_sync();
         tc::tmem_dealloc(tmem, TMEM_COLS);
@@ -431,7 +540,7 @@ prefill_attn_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
 
 template <typename T>
 rfsn_status launch(const CUtensorMap* maps, const PrefillParams& p, cudaStream_t stream) {
-    const size_t smem = sizeof(Smem) + 1024;
+    const size_t smem = sizeof(Smem);
     auto kern = prefill_attn_kernel<T>;
     RFSN_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     const int ppc = BM / p.groups_per_kv;
