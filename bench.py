@@ -26,6 +26,10 @@ roofline against the measured HBM copy bandwidth, NVML clock samples taken
 during the timed region, and (N = 1) a CPU baseline: the reference algorithm
 restated in numpy, on the host's cores. ``--impl reference`` prints that CPU
 arm alone.
+
+At N = 1 the line also carries ``secondary`` (the 8K fp16 decode workload)
+and ``prefill``: one layer of a 32K-token prompt prefilled in 2048-token
+chunks on the tcgen05 tensor-core kernel, against the measured bf16 peak.
 """
 
 from __future__ import annotations
@@ -422,10 +426,13 @@ def run_ours(args, w):
             traffic = None
 
     secondary = None
+    prefill = None
     cpu = None
     if world == 1 and rank == 0:
         if args.workload == "decode128k_bf16" and not args.no_secondary:
             secondary = secondary_8k(args, device, peak)
+        if not args.no_prefill:
+            prefill = prefill_32k(args, device)
         if not args.no_cpu_baseline:
             sec, n, threads = cpu_baseline_sample(w)
             cpu = {
@@ -491,6 +498,8 @@ def run_ours(args, w):
             line["cpu_baseline"] = cpu
         if secondary is not None:
             line["secondary"] = secondary
+        if prefill is not None:
+            line["prefill"] = prefill
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
@@ -550,6 +559,103 @@ def secondary_8k(args, device, peak):
     }
 
 
+PREFILL_DESC = ("one layer of a 32,768-token prompt prefilled in 16 chunks of 2,048 tokens, 32 q / 8 kv heads, head_dim "
+                "128, bf16 K/V; hot ring 4,096 tokens, so chunk c attends to c-1 archived 2,048-token blocks plus the "
+                "hot window (the previous chunk and itself), causally")
+
+
+def bf16_peak() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["bf16_tflops"]), "measured (cuBLAS bf16 burst)"
+        except Exception:
+            pass
+    return 1590.0, "fallback"
+
+
+def prefill_32k(args, device):
+    """Chunked-prefill attention on the tcgen05 kernel: the 16 chunk calls of one
+    layer, K/V resident in HBM, timed with CUDA events. Useful FLOPs count the
+    causal products once (4 * heads * head_dim per query-key pair); the kernel
+    issues twice that on the tensor cores (16-bit high + residual parts of q and P)."""
+    import ctypes
+
+    import torch
+
+    from rfsn_b200 import _native as native
+
+    H, Hkv, D, chunk, cap, n_chunks = 32, 8, 128, 2048, 4096, 16
+    n_blocks_max = n_chunks - 2
+    rows = cap + n_blocks_max * chunk
+    gen = torch.Generator(device=device).manual_seed(5)
+    k = torch.randn((Hkv, rows, D), generator=gen, device=device).to(torch.bfloat16)
+    v = torch.randn((Hkv, rows, D), generator=gen, device=device).to(torch.bfloat16)
+    q = torch.randn((1, H, chunk, D), generator=gen, device=device)
+    out = torch.empty_like(q)
+    lse = torch.empty((1, H, chunk), device=device)
+    arena = native.Arena(k, v)
+    recs = torch.zeros((n_blocks_max + 1, 4), dtype=torch.int32)
+    tile = 0
+    for i in range(n_blocks_max):
+        recs[i] = torch.tensor([cap + i * chunk, i * chunk, chunk, tile], dtype=torch.int32)
+        tile += chunk // 64
+    recs_d = recs.to(device)
+    nbytes = native.workspace_bytes(1, H, Hkv, chunk, D, 0)
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+    calls, flops = [], 0.0
+    for c in range(n_chunks):
+        nb = max(0, c - 1)
+        hot_start = nb * chunk
+        hot_len = min(c + 1, 2) * chunk
+        table = native.PageTableC(recs_d.data_ptr(), nb, nb * chunk, nb * (chunk // 64), 0)
+        hot = native.HotWindowC(0, cap, hot_start % cap, hot_len, hot_start)
+        calls.append((table, hot, c * chunk))
+        flops += 4.0 * H * D * (chunk * c * chunk + chunk * (chunk + 1) / 2)
+    lib = native.lib()
+
+    def run_layer():
+        for table, hot, pos in calls:
+            native.check(lib.rfsn_paged_attention(arena.handle, q.data_ptr(), 1, H, Hkv, chunk, pos, ctypes.byref(table),
+                                                  ctypes.byref(hot), out.data_ptr(), lse.data_ptr(), ws.data_ptr(),
+                                                  nbytes, 0, native.stream_ptr()), "prefill")
+
+    for _ in range(2):
+        run_layer()
+    torch.cuda.synchronize()
+    reps = max(3, min(args.steps, 10))
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(reps):
+        run_layer()
+    end.record()
+    end.synchronize()
+    native.check(lib.rfsn_workspace_check(ws.data_ptr(), native.stream_ptr(), 30_000_000), "prefill workspace")
+    ms = start.elapsed_time(end) / reps
+    arena.close()
+    tflops = flops / (ms / 1e3) / 1e12
+    peak, kind = bf16_peak()
+    return {
+        "workload": "prefill32k_chunk2048_bf16",
+        "desc": PREFILL_DESC,
+        "value": 32768 / (ms / 1e3),
+        "unit": "prompt tokens/s (one layer's attention)",
+        "ms_per_layer": ms,
+        "useful_tflop_per_layer": flops / 1e12,
+        "roofline": {
+            "bound": "tensor",
+            "achieved": tflops,
+            "peak": peak,
+            "unit": "TFLOP/s",
+            "frac": tflops / peak,
+            "peak_kind": kind,
+            "tensor_work_factor": 2,
+            "kernel": "rfsn::prefill::prefill_attn_kernel (tcgen05, TMEM accumulators)",
+        },
+        "l2": "K/V 67 MB + q/out per call; every chunk streams its whole causal context",
+    }
+
+
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -560,6 +666,7 @@ def main() -> int:
     ap.add_argument("--calls-per-step", type=int, default=200)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the chunked-prefill measurement (N = 1)")
     ap.add_argument("--merge", choices=["p2p", "nccl"], default="p2p",
                     help="cross-GPU merge for N > 1: fused NVLink mailboxes (default) or NCCL all-gather")
     args = ap.parse_args()
