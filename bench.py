@@ -559,6 +559,7 @@ def secondary_8k(args, device, peak):
     }
 
 
+PREFILL_WORKLOAD = "prefill32k_chunk2048_bf16"
 PREFILL_DESC = ("one layer of a 32,768-token prompt prefilled in 16 chunks of 2,048 tokens, 32 q / 8 kv heads, head_dim "
                 "128, bf16 K/V; hot ring 4,096 tokens, so chunk c attends to c-1 archived 2,048-token blocks plus the "
                 "hot window (the previous chunk and itself), causally")
@@ -656,13 +657,31 @@ def prefill_32k(args, device):
     }
 
 
+def run_prefill(args):
+    """``--workload prefill32k_chunk2048_bf16``: the chunked-prefill measurement as
+    its own line (1 GPU; the reference arm has no GPU counterpart)."""
+    import torch
+
+    if args.impl == "reference":
+        print(json.dumps({"impl": "reference", "unavailable": "the prefill workload is measured on the GPU arm only; "
+                          "the reference CPU arm times the decode workloads"}), flush=True)
+        return 0
+    torch.cuda.set_device(0)
+    r = prefill_32k(args, torch.device("cuda", 0))
+    line = {"metric": "chunked-prefill attention prompt tokens/s and TFLOP/s (tensor roofline)", "n_gpus": 1,
+            "steps": max(3, min(args.steps, 10)), "warmup": 2, "higher_is_better": True, "dtype": "bf16",
+            "data": "synthetic N(0,1) q/K/V (seeded); K/V resident in HBM", **r}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode128k_bf16")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + [PREFILL_WORKLOAD], default="decode128k_bf16")
     ap.add_argument("--calls-per-step", type=int, default=200)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true")
@@ -672,6 +691,8 @@ def main() -> int:
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
+    if args.workload == PREFILL_WORKLOAD:
+        return run_prefill(args)
     w = WORKLOADS[args.workload]
     if args.impl == "reference":
         return run_reference(args, w)
