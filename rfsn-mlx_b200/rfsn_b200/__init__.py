@@ -2,7 +2,8 @@
 
 Module layout mirrors the reference package ``rfsn_v10_5`` for the path it
 replaces: ``config``, ``block_manager``, ``storage``, ``residency``,
-``cache``, ``attention_exact`` and the attention step of ``layer``. Tensors
+``cache``, ``attention_exact``, the attention step of ``layer`` and the
+``model`` driver (dense parts in torch). Tensors
 are torch CUDA tensors; the compute runs in ``librfsn_b200.so`` (sm_100a),
 bound through ``_native``. Multi-GPU sharded decode lives in ``sharded``.
 """
@@ -21,6 +22,7 @@ from .attention_exact import (  # noqa: F401
     run_segmented_attention,
 )
 from .layer import attention_step, build_rope_tables  # noqa: F401
+from .model import RFSNMLX, RFSNModel  # noqa: F401
 
 __all__ = [
     "RFSNConfig",
@@ -44,4 +46,6 @@ __all__ = [
     "exact_prefill_attention",
     "exact_decode_attention",
     "build_causal_mask",
+    "RFSNModel",
+    "RFSNMLX",
 ]

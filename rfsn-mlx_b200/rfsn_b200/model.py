@@ -1,0 +1,278 @@
+"""Model driver (drop-in for ``rfsn_v10_5.model.RFSNMLX``, model.py:43-336).
+
+The transformer around the attention path: token embedding, per layer
+RMSNorm -> q/k/v projections -> attention step -> o_proj + residual ->
+RMSNorm -> SwiGLU FFN + residual (layer.py:53-167), final LayerNorm and a
+weight-tied LM head (model.py:56-69). Prefill runs in chunks of
+``min(hot_capacity, L)`` tokens at ``start_pos = cache.layer(0).hot_end``
+(model.py:133-165); decode validates ``pos == hot_end`` (model.py:89-104).
+
+The attention step of every layer is ``layer.attention_step``: RoPE fused
+with the ring append, the seal rule, the decode prefetch hook and exact
+attention over archived blocks + hot window on the CUDA kernels. The dense
+projections, norms and FFN are plain torch operations on the same device.
+
+Parameter names follow the reference's ``tree_flatten(model.parameters())``
+(``embed_tokens.weight``, ``layers.{i}.q_proj.weight``, ...,
+``layers.{i}.attn_norm.weight``, ``norm.weight``, ``norm.bias``) so weights
+load unchanged. Activations stay in the model dtype (the float32 attention
+output is cast back before ``o_proj``); for a float32 model this is the
+reference's dtype flow.
+"""
+
+from __future__ import annotations
+
+from typing import Dict, Iterable, List, Mapping, Optional, Tuple, Union
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+from .cache import RFSNCache
+from .config import RFSNConfig, RuntimeMode, resolve_dtype
+from .layer import attention_step
+
+ArrayLike = Union[np.ndarray, torch.Tensor]
+
+
+def _rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    """layer.py:52-64: weight * x / sqrt(mean(x^2) + eps), computed in float32."""
+    xf = x.float()
+    rms = torch.sqrt(torch.mean(xf * xf, dim=-1, keepdim=True) + eps)
+    return (weight.float() * (xf / rms)).to(x.dtype)
+
+
+def _layer_norm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float) -> torch.Tensor:
+    """model.py:65 (nn.LayerNorm): (x - mean) / sqrt(var + eps) * weight + bias."""
+    return F.layer_norm(x.float(), (x.shape[-1],), weight.float(), bias.float(), eps).to(x.dtype)
+
+
+class RFSNLayer:
+    """One transformer layer (layer.py:67-167) with the attention step on the CUDA path."""
+
+    def __init__(self, config: RFSNConfig, layer_idx: int, params: Dict[str, torch.Tensor]) -> None:
+        self.config = config
+        self.layer_idx = layer_idx
+        self.p = params  # views into the model's parameter dict for this layer
+
+    def _w(self, name: str) -> torch.Tensor:
+        return self.p[f"layers.{self.layer_idx}.{name}"]
+
+    def __call__(self, x: torch.Tensor, layer_cache, start_pos: int) -> torch.Tensor:
+        cfg = self.config
+        B, L, _ = x.shape
+        H, Hkv, D = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
+        residual = x
+        xn = _rms_norm(x, self._w("attn_norm.weight"), cfg.norm_eps)
+        q = F.linear(xn, self._w("q_proj.weight")).reshape(B, L, H, D).transpose(1, 2)
+        k = F.linear(xn, self._w("k_proj.weight")).reshape(B, L, Hkv, D).transpose(1, 2)
+        v = F.linear(xn, self._w("v_proj.weight")).reshape(B, L, Hkv, D).transpose(1, 2)
+        attn = attention_step(q, k, v, layer_cache, start_pos)  # float32 [B, H, L, D]
+        attn = attn.transpose(1, 2).reshape(B, L, H * D).to(x.dtype)
+        x = residual + F.linear(attn, self._w("o_proj.weight"))
+        h = _rms_norm(x, self._w("ffn_norm.weight"), cfg.norm_eps)
+        ffn = F.linear(F.silu(F.linear(h, self._w("gate_proj.weight"))) * F.linear(h, self._w("up_proj.weight")),
+                       self._w("down_proj.weight"))
+        return x + ffn
+
+
+class RFSNModel:
+    """Full RFSN transformer (model.py:43-336)."""
+
+    def __init__(self, config: RFSNConfig, *, device: Optional[Union[str, torch.device]] = None,
+                 seed: Optional[int] = None) -> None:
+        self.config = config
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.dtype = resolve_dtype(config.model_dtype)
+        self.params: Dict[str, torch.Tensor] = {}
+        gen = torch.Generator(device="cpu")
+        gen.manual_seed(0 if seed is None else seed)
+        for name, shape in self.parameter_shapes().items():
+            if name.endswith("norm.weight"):
+                t = torch.ones(shape)
+            elif name == "norm.bias":
+                t = torch.zeros(shape)
+            else:
+                t = torch.empty(shape).normal_(0.0, 0.02, generator=gen)
+            self.params[name] = t.to(device=self.device, dtype=self.dtype)
+        self.layers = [RFSNLayer(config, i, self.params) for i in range(config.num_layers)]
+
+    # ------------------------------------------------------------------ parameters
+    def parameter_shapes(self) -> Dict[str, Tuple[int, ...]]:
+        cfg = self.config
+        Hd, H, Hkv, D, Fd = cfg.hidden_dim, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, cfg.ffn_dim
+        shapes = {"embed_tokens.weight": (cfg.vocab_size, Hd), "norm.weight": (Hd,), "norm.bias": (Hd,)}
+        for i in range(cfg.num_layers):
+            pre = f"layers.{i}."
+            shapes.update({
+                pre + "q_proj.weight": (H * D, Hd), pre + "k_proj.weight": (Hkv * D, Hd),
+                pre + "v_proj.weight": (Hkv * D, Hd), pre + "o_proj.weight": (Hd, H * D),
+                pre + "gate_proj.weight": (Fd, Hd), pre + "up_proj.weight": (Fd, Hd),
+                pre + "down_proj.weight": (Hd, Fd),
+                pre + "attn_norm.weight": (Hd,), pre + "ffn_norm.weight": (Hd,),
+            })
+        return shapes
+
+    def parameters(self) -> Dict[str, torch.Tensor]:
+        return dict(self.params)
+
+    def load_weights(self, weights: Union[Mapping[str, ArrayLike], Iterable[Tuple[str, ArrayLike]]],
+                     strict: bool = False) -> "RFSNModel":
+        """Load named weights (reference parameter names); ``strict`` requires every parameter."""
+        items = weights.items() if isinstance(weights, Mapping) else list(weights)
+        shapes = self.parameter_shapes()
+        seen = set()
+        for name, value in items:
+            if name not in shapes:
+                raise ValueError(f"Received parameter not in model: {name}")
+            t = torch.as_tensor(np.asarray(value)) if isinstance(value, np.ndarray) else torch.as_tensor(value)
+            if tuple(t.shape) != shapes[name]:
+                raise ValueError(f"Expected shape {shapes[name]} for parameter {name} but received shape {tuple(t.shape)}")
+            self.params[name].copy_(t.to(device=self.device, dtype=self.dtype))
+            seen.add(name)
+        if strict:
+            missing = sorted(set(shapes) - seen)
+            if missing:
+                raise ValueError(f"Missing parameters: {missing}")
+        return self
+
+    # ------------------------------------------------------------------ driver
+    def _lm_head(self, x: torch.Tensor) -> torch.Tensor:
+        """model.py:67-69: weight-tied head x @ E^T."""
+        return x @ self.params["embed_tokens.weight"].T
+
+    def _context_end(self, cache: RFSNCache) -> int:
+        return cache.layer(0).hot_end
+
+    def _validate_prefill_bounds(self, cache: RFSNCache, incoming_tokens: int) -> int:
+        """model.py:74-87 (same messages)."""
+        context_end = self._context_end(cache)
+        projected = context_end + incoming_tokens
+        cfg = self.config
+        if cfg.max_position_embeddings > 0 and projected > cfg.max_position_embeddings:
+            raise ValueError(
+                f"Prompt would exceed max_position_embeddings={cfg.max_position_embeddings} "
+                f"(requested {projected} tokens total)"
+            )
+        if cfg.runtime_mode == RuntimeMode.EXACT and projected > cfg.hot_capacity:
+            raise RuntimeError(
+                "runtime_mode='exact' is hot-window only; the prompt would exceed "
+                f"hot_capacity={cfg.hot_capacity}"
+            )
+        return context_end
+
+    def _validate_decode_bounds(self, cache: RFSNCache, pos: int) -> None:
+        """model.py:89-104 (same messages)."""
+        context_end = self._context_end(cache)
+        if pos != context_end:
+            raise ValueError(f"decode_step expected pos={context_end} from cache state, got pos={pos}")
+        projected = pos + 1
+        cfg = self.config
+        if cfg.max_position_embeddings > 0 and projected > cfg.max_position_embeddings:
+            raise ValueError(f"Decode would exceed max_position_embeddings={cfg.max_position_embeddings}")
+        if cfg.runtime_mode == RuntimeMode.EXACT and projected > cfg.hot_capacity:
+            raise RuntimeError(
+                "runtime_mode='exact' is hot-window only; the decode step would exceed "
+                f"hot_capacity={cfg.hot_capacity}"
+            )
+
+    def _embed(self, tokens: torch.Tensor) -> torch.Tensor:
+        return F.embedding(tokens.to(device=self.device, dtype=torch.long), self.params["embed_tokens.weight"])
+
+    def _forward(self, x: torch.Tensor, cache: RFSNCache, start_pos: int) -> torch.Tensor:
+        """model.py:106-131."""
+        for i, layer in enumerate(self.layers):
+            x = layer(x, cache.layer(i), start_pos)
+        x = _layer_norm(x, self.params["norm.weight"], self.params["norm.bias"], self.config.norm_eps)
+        return self._lm_head(x)
+
+    def prefill(self, tokens: ArrayLike, cache: RFSNCache) -> torch.Tensor:
+        """model.py:133-165: tokens (B, L) int -> logits (B, L, vocab)."""
+        tokens = torch.as_tensor(np.asarray(tokens)) if isinstance(tokens, np.ndarray) else tokens
+        seq_len = int(tokens.shape[1])
+        if seq_len == 0:
+            raise ValueError("prefill requires at least one token")
+        self._validate_prefill_bounds(cache, seq_len)
+        chunk_size = max(1, min(self.config.hot_capacity, seq_len))
+        out: List[torch.Tensor] = []
+        chunk_start = 0
+        while chunk_start < seq_len:
+            chunk_end = min(seq_len, chunk_start + chunk_size)
+            start_pos = self._context_end(cache)
+            x = self._embed(tokens[:, chunk_start:chunk_end])
+            out.append(self._forward(x, cache, start_pos))
+            chunk_start = chunk_end
+        return out[0] if len(out) == 1 else torch.cat(out, dim=1)
+
+    def decode_step(self, token_id: ArrayLike, cache: RFSNCache, pos: int) -> torch.Tensor:
+        """model.py:167-189: token_id (B,) -> logits (B, vocab)."""
+        self._validate_decode_bounds(cache, pos)
+        token_id = torch.as_tensor(np.asarray(token_id)) if isinstance(token_id, np.ndarray) else token_id
+        x = self._embed(token_id.reshape(-1, 1))
+        return self._forward(x, cache, pos)[:, 0, :]
+
+    def generate(self, prompt_ids: ArrayLike, max_new_tokens: int, cache: Optional[RFSNCache] = None,
+                 temperature: float = 1.0, top_p: float = 1.0, top_k: int = 0, repetition_penalty: float = 1.0,
+                 generator: Optional[torch.Generator] = None) -> List[torch.Tensor]:
+        """model.py:191-264: prefill, then ``max_new_tokens - 1`` decode steps."""
+        prompt_ids = torch.as_tensor(np.asarray(prompt_ids)) if isinstance(prompt_ids, np.ndarray) else prompt_ids
+        B, L = int(prompt_ids.shape[0]), int(prompt_ids.shape[1])
+        if cache is None:
+            cache = RFSNCache(self.config, batch_size=B, device=self.device)
+        cfg = self.config
+        requested_total = self._context_end(cache) + L + max_new_tokens
+        if cfg.max_position_embeddings > 0 and requested_total > cfg.max_position_embeddings:
+            raise ValueError(
+                "Prompt plus requested generation would exceed "
+                f"max_position_embeddings={cfg.max_position_embeddings}"
+            )
+        if cfg.runtime_mode == RuntimeMode.EXACT and requested_total > cfg.hot_capacity:
+            raise RuntimeError(
+                "runtime_mode='exact' is hot-window only; prompt plus requested generation would exceed "
+                f"hot_capacity={cfg.hot_capacity}"
+            )
+        seen = prompt_ids.to(self.device, torch.long)
+        logits = self.prefill(prompt_ids, cache)
+        nxt = self._sample(logits[:, -1, :], temperature, top_p, top_k, repetition_penalty, seen, generator)
+        generated = [nxt]
+        seen = torch.cat([seen, nxt[:, None].long()], dim=1)
+        pos = L
+        for _ in range(max_new_tokens - 1):
+            logits = self.decode_step(nxt, cache, pos)
+            nxt = self._sample(logits, temperature, top_p, top_k, repetition_penalty, seen, generator)
+            generated.append(nxt)
+            seen = torch.cat([seen, nxt[:, None].long()], dim=1)
+            pos += 1
+        return generated
+
+    @staticmethod
+    def _sample(logits: torch.Tensor, temperature: float, top_p: float, top_k: int, repetition_penalty: float,
+                seen_ids: torch.Tensor, generator: Optional[torch.Generator] = None) -> torch.Tensor:
+        """model.py:266-336: greedy at temperature 0, else repetition penalty,
+        top-k, temperature, top-p (nucleus) and a categorical draw."""
+        if temperature == 0.0:
+            return torch.argmax(logits, dim=-1).to(torch.int32)
+        logits = logits.float()
+        if repetition_penalty != 1.0:
+            mask = torch.zeros_like(logits)
+            mask.scatter_(1, seen_ids.long(), 1.0)
+            factor = mask * (repetition_penalty - 1.0) + 1.0
+            logits = torch.where(logits > 0, logits / factor, logits * factor)
+        if top_k > 0:
+            threshold = torch.topk(logits, top_k, dim=-1).values[:, -1:]
+            logits = torch.where(logits >= threshold, logits, torch.full_like(logits, float("-inf")))
+        scaled = logits / temperature
+        if top_p < 1.0:
+            probs = torch.softmax(scaled, dim=-1)
+            sorted_probs, sorted_idx = torch.sort(probs, dim=-1, descending=True)
+            cumsum = torch.cumsum(sorted_probs, dim=-1)
+            keep = (cumsum - sorted_probs) < top_p
+            sorted_probs = sorted_probs * keep
+            sorted_probs = sorted_probs / sorted_probs.sum(dim=-1, keepdim=True)
+            local = torch.multinomial(sorted_probs, 1, generator=generator)
+            return torch.gather(sorted_idx, 1, local)[:, 0].to(torch.int32)
+        probs = torch.softmax(scaled, dim=-1)
+        return torch.multinomial(probs, 1, generator=generator)[:, 0].to(torch.int32)
+
+
+RFSNMLX = RFSNModel  # the reference's class name

@@ -1,0 +1,199 @@
+"""Model-level parity on the GPU: the tiny CPU-runnable configuration (1 layer,
+hidden 128, 2/2 heads, head_dim 64, float32, hot ring 8, blocks of 4) driven by
+``rfsn_b200.model`` with the reference's weights, prompt and greedy decode,
+against the logits, tokens and ring/page-table states the reference produced
+(``tests/golden/tiny_model_golden.npz``). Attention runs on the CUDA kernels
+(float32 cache -> CUDA-core kernel); prefill and 8 decode steps seal archived
+blocks, so the segmented path is exercised."""
+
+import numpy as np
+import pytest
+import torch
+
+from _util import GOLDEN
+from test_model_cpu import tiny_config
+
+pytestmark = pytest.mark.gpu
+ATOL = 2e-3  # north-star bar for logits
+GUARD = 1e-4  # float32 end to end: observed ~1e-6
+
+
+def _state(cache):
+    lc = cache.layer(0)
+    return [lc.hot_head_index, lc.hot_seq_len, lc.hot_start] + [
+        x for m in lc.block_manager.iter_blocks(layer_id=0) for x in (m.logical_start, m.logical_end)
+    ]
+
+
+def test_tiny_model_matches_reference_logits_tokens_and_ring(tmp_path):
+    from rfsn_b200.cache import RFSNCache
+    from rfsn_b200.model import RFSNModel
+
+    g = np.load(GOLDEN / "tiny_model_golden.npz")
+    cfg = tiny_config(tmp_path)
+    model = RFSNModel(cfg, device="cuda")
+    model.load_weights({k[2:]: g[k] for k in g.files if k.startswith("w/")})
+    cache = RFSNCache(cfg, batch_size=1, device="cuda")
+    ring = g["ring_states"]
+
+    logits = model.prefill(g["prompt"], cache)
+    err = float(np.abs(logits.cpu().numpy() - g["prefill_logits"]).max())
+    assert err <= ATOL and err <= GUARD, err
+    st = _state(cache)
+    assert st == [int(x) for x in ring[0][:len(st)]] and all(x == -1 for x in ring[0][len(st):])
+
+    token = torch.argmax(logits[:, -1, :], dim=-1).to(torch.int32)
+    tokens = [int(token[0])]
+    pos = 8
+    for step in range(8):
+        out = model.decode_step(token, cache, pos)
+        err = float(np.abs(out.cpu().numpy() - g["decode_logits"][step]).max())
+        assert err <= ATOL and err <= GUARD, (step, err)
+        st = _state(cache)
+        assert st == [int(x) for x in ring[step + 1][:len(st)]], (step, st)
+        token = torch.argmax(out, dim=-1).to(torch.int32)
+        tokens.append(int(token[0]))
+        pos += 1
+    assert tokens == [int(t) for t in g["tokens"]]
+
+
+def test_generate_greedy_equals_stepwise(tmp_path):
+    from rfsn_b200.cache import RFSNCache
+    from rfsn_b200.model import RFSNModel
+
+    g = np.load(GOLDEN / "tiny_model_golden.npz")
+    cfg = tiny_config(tmp_path, session_id="tiny-gen")
+    model = RFSNModel(cfg, device="cuda")
+    model.load_weights({k[2:]: g[k] for k in g.files if k.startswith("w/")})
+    out = model.generate(g["prompt"], 9, cache=RFSNCache(cfg, batch_size=1, device="cuda"), temperature=0.0)
+    assert [int(t[0]) for t in out] == [int(t) for t in g["tokens"]]
+
+
+def test_bf16_model_prefill_chunks_and_decode_run_on_tensor_core_paths(tmp_path, monkeypatch):
+    """A larger bf16 model (head_dim 128, GQA 4, 2 layers, hot ring 256, blocks of
+    128): prefill chunks of 256/256/88 tokens go to the tcgen05 prefill kernel and
+    decode steps to the split-KV decode kernel, over sealed archived blocks and a
+    wrapped ring. Every attention call the model makes is checked against dense
+    float32 attention over the full history of the same q/k/v (1e-4). A bf16
+    network turns ~1e-6 differences into ulp-level noise downstream, so the logits
+    are only checked against a dense re-computation to a few bf16 ulps."""
+    import rfsn_b200.model as M
+    from rfsn_b200.cache import RFSNCache
+    from rfsn_b200.config import RFSNConfig, RuntimeMode
+
+    calls = []
+    orig = M.attention_step
+
+    def recording(q, k, v, layer_cache, start_pos):
+        out = orig(q, k, v, layer_cache, start_pos)
+        calls.append((layer_cache.layer_id, q.detach().clone(), k.detach().clone(), v.detach().clone(), start_pos,
+                      out.detach().clone()))
+        return out
+
+    monkeypatch.setattr(M, "attention_step", recording)
+    cfg = RFSNConfig(hidden_dim=1024, num_heads=8, num_kv_heads=2, head_dim=128, num_layers=2, vocab_size=256,
+                     hot_capacity=256, block_size_seq=128, warm_capacity=4096, rope_base=10000.0, ffn_multiplier=2,
+                     model_dtype="bfloat16", runtime_mode=RuntimeMode.ARCHIVED, disk_cache_dir=str(tmp_path),
+                     session_id="bf16")
+    model = M.RFSNModel(cfg, device="cuda", seed=7)
+    cache = RFSNCache(cfg, batch_size=1, device="cuda")
+    dense = _DenseModel(model)
+    prompt = torch.randint(0, 256, (1, 600), generator=torch.Generator().manual_seed(8))
+    logits = model.prefill(prompt, cache)
+    ref = torch.cat([dense(prompt[:, a:b]) for a, b in ((0, 256), (256, 512), (512, 600))], dim=1)
+    _close_bf16(logits[0].float(), ref[0])
+    tok = torch.argmax(logits[:, -1], dim=-1)
+    for pos in range(600, 604):
+        out = model.decode_step(tok, cache, pos)
+        ref = dense(tok.reshape(1, 1).cpu())[:, -1]
+        _close_bf16(out[0].float(), ref[0])
+        tok = torch.argmax(out, dim=-1)
+    assert len(calls) == 2 * (3 + 4)
+    assert [c[1].shape[2] for c in calls[::2]] == [256, 256, 88, 1, 1, 1, 1]
+
+    hist = {}
+    for layer_id, q, k, v, start_pos, out in calls:
+        kr = _rope(k, start_pos, cfg).to(torch.bfloat16).float()
+        kh, vh = hist.get(layer_id, (None, None))
+        kh = kr if kh is None else torch.cat([kh, kr], dim=2)
+        vh = v.float() if vh is None else torch.cat([vh, v.float()], dim=2)
+        hist[layer_id] = (kh, vh)
+        qr = _rope(q, start_pos, cfg)
+        G = cfg.num_heads // cfg.num_kv_heads
+        s = qr @ kh.repeat_interleave(G, 1).transpose(-1, -2) / cfg.head_dim ** 0.5
+        L, T = q.shape[2], kh.shape[2]
+        qpos = torch.arange(start_pos, start_pos + L, device=q.device)[:, None]
+        s = s.masked_fill(torch.arange(T, device=q.device)[None, :] > qpos, float("-inf"))
+        want = torch.softmax(s, dim=-1) @ vh.repeat_interleave(G, 1)
+        err = float((out - want).abs().max())
+        assert err <= 1e-4, (layer_id, start_pos, L, err)
+
+
+def _rope(t, start_pos, cfg):
+    from rfsn_b200.layer import build_rope_tables
+
+    D = cfg.head_dim
+    cos, sin = build_rope_tables(D, cfg.rope_base, t.shape[2], start_pos, device=t.device)
+    t = t.float()
+    rot = torch.cat([-t[..., D // 2:], t[..., :D // 2]], dim=-1)
+    return t * cos + rot * sin
+
+
+def _close_bf16(got, ref):
+    ulp = 2.0 ** -7 * float(ref.abs().max())  # bf16 spacing at the largest logit
+    diff = (got - ref).abs()
+    assert float(diff.max()) <= 4 * ulp, (float(diff.max()), ulp)
+    assert float(diff.mean()) <= ulp / 2, (float(diff.mean()), ulp)
+
+
+class _DenseModel:
+    """The same network with plain dense attention (float32 softmax over all
+    previous K/V, GQA by head mapping), fed the same chunks as the model so
+    every projection runs with the same shapes (identical cuBLAS results); only
+    the attention differs."""
+
+    def __init__(self, model):
+        self.m = model
+        self.k = [None] * model.config.num_layers
+        self.v = [None] * model.config.num_layers
+        self.pos = 0
+
+    def __call__(self, toks):
+        import torch.nn.functional as F
+
+        from rfsn_b200.layer import build_rope_tables
+        from rfsn_b200.model import _layer_norm, _rms_norm
+
+        m, cfg, p = self.m, self.m.config, self.m.params
+        L = toks.shape[1]
+        H, Hkv, D = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
+        cos, sin = build_rope_tables(D, cfg.rope_base, L, self.pos, device=m.device)
+
+        def rope(t):
+            t = t.float()
+            rot = torch.cat([-t[..., D // 2:], t[..., :D // 2]], dim=-1)
+            return t * cos + rot * sin
+
+        x = F.embedding(toks.to(m.device).long(), p["embed_tokens.weight"])
+        for i in range(cfg.num_layers):
+            w = lambda n: p[f"layers.{i}.{n}"]  # noqa: E731
+            xn = _rms_norm(x, w("attn_norm.weight"), cfg.norm_eps)
+            q = rope(F.linear(xn, w("q_proj.weight")).reshape(1, L, H, D).transpose(1, 2))
+            k = rope(F.linear(xn, w("k_proj.weight")).reshape(1, L, Hkv, D).transpose(1, 2)).to(m.dtype).float()
+            v = F.linear(xn, w("v_proj.weight")).reshape(1, L, Hkv, D).transpose(1, 2).to(m.dtype).float()
+            self.k[i] = k if self.k[i] is None else torch.cat([self.k[i], k], dim=2)
+            self.v[i] = v if self.v[i] is None else torch.cat([self.v[i], v], dim=2)
+            kk = self.k[i].repeat_interleave(H // Hkv, dim=1)
+            vv = self.v[i].repeat_interleave(H // Hkv, dim=1)
+            T = kk.shape[2]
+            s = q @ kk.transpose(-1, -2) / D ** 0.5
+            qpos = torch.arange(self.pos, self.pos + L, device=m.device)[:, None]
+            s = s.masked_fill(torch.arange(T, device=m.device)[None, :] > qpos, float("-inf"))
+            a = (torch.softmax(s, dim=-1) @ vv).transpose(1, 2).reshape(1, L, H * D).to(x.dtype)
+            x = x + F.linear(a, w("o_proj.weight"))
+            h = _rms_norm(x, w("ffn_norm.weight"), cfg.norm_eps)
+            x = x + F.linear(F.silu(F.linear(h, w("gate_proj.weight"))) * F.linear(h, w("up_proj.weight")),
+                             w("down_proj.weight"))
+        x = _layer_norm(x, p["norm.weight"], p["norm.bias"], cfg.norm_eps)
+        self.pos += L
+        return (x @ p["embed_tokens.weight"].T).float()
