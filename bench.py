@@ -657,6 +657,76 @@ def prefill_32k(args, device):
     }
 
 
+MODEL_WORKLOAD = "model8b_e2e_bf16"
+MODEL_DESC = ("Llama-3-8B-shaped model, random init normal(0, 0.02) seed 4: 32 layers, hidden 4096, 32 q / 8 kv "
+              "heads, head_dim 128, SwiGLU FFN 14336, vocab 128256, RoPE theta 500000, bf16; 4,096-token prompt of "
+              "uniform random ids prefilled in slices of 512, then 256 greedy decode steps; hot ring 2,048, blocks "
+              "of 256, warm capacity 8,192 (every archived block stays in HBM)")
+
+
+def run_model(args):
+    """``--workload model8b_e2e_bf16``: whole-model prefill and greedy decode through
+    ``rfsn_b200.model`` (dense layers in torch/cuBLAS, attention on this
+    library's kernels). Timed with CUDA events; decode includes the argmax and
+    the host-side cache logic of every step."""
+    import torch
+
+    from rfsn_b200.cache import RFSNCache
+    from rfsn_b200.config import RFSNConfig, RuntimeMode
+    from rfsn_b200.model import RFSNModel
+
+    if args.impl == "reference":
+        print(json.dumps({"impl": "reference", "unavailable": "the 8B-shaped model needs a GPU; the reference CPU "
+                          "arm times the decode-attention workloads"}), flush=True)
+        return 0
+    torch.cuda.set_device(0)
+    device = torch.device("cuda", 0)
+    with tempfile.TemporaryDirectory() as tmp:
+        cfg = RFSNConfig(hidden_dim=4096, num_heads=32, num_kv_heads=8, head_dim=128, num_layers=32,
+                         vocab_size=128256, ffn_dim=14336, rope_base=500000.0, norm_eps=1e-5, model_dtype="bfloat16",
+                         hot_capacity=2048, block_size_seq=256, warm_capacity=8192, cold_capacity=16384,
+                         runtime_mode=RuntimeMode.ARCHIVED, disk_cache_dir=tmp, session_id="bench")
+        model = RFSNModel(cfg, device=device, seed=4)
+        gen = torch.Generator().manual_seed(4)
+        prompt = torch.randint(0, cfg.vocab_size, (1, 4096), generator=gen, dtype=torch.int32)
+        n_decode = 256
+
+        def one_run():
+            cache = RFSNCache(cfg, batch_size=1, device=device)
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            ev[0].record()
+            logits = None
+            for a in range(0, 4096, 512):
+                logits = model.prefill(prompt[:, a:a + 512], cache)
+            ev[1].record()
+            tok = torch.argmax(logits[:, -1, :], dim=-1).to(torch.int32)
+            toks = [tok]
+            for pos in range(4096, 4096 + n_decode - 1):
+                out = model.decode_step(tok, cache, pos)
+                tok = torch.argmax(out, dim=-1).to(torch.int32)
+                toks.append(tok)
+            ev[2].record()
+            ev[2].synchronize()
+            blocks = sum(1 for _ in cache.layer(0).block_manager.iter_blocks(layer_id=0))
+            return ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2]), blocks, torch.stack(toks).cpu()
+
+        one_run()  # warm-up (cuBLAS heuristics, allocator, kernels)
+        pre_ms, dec_ms, blocks, toks = one_run()
+    line = {
+        "metric": "model end-to-end prefill and decode tokens/s (Llama-3-8B shape, bf16)",
+        "workload": MODEL_WORKLOAD, "desc": MODEL_DESC, "n_gpus": 1, "dtype": "bf16",
+        "data": "synthetic: random weights and prompt ids (seeded)", "higher_is_better": True,
+        "value": (n_decode - 1) / (dec_ms / 1e3), "unit": "decode tokens/s",
+        "decode_ms_per_token": dec_ms / (n_decode - 1),
+        "prefill_tokens_per_s": 4096 / (pre_ms / 1e3), "prefill_ms": pre_ms,
+        "archived_blocks_after": blocks,
+        "notes": "dense projections/norms/FFN/LM head are torch (cuBLAS) ops; attention (RoPE+append, seal, paged "
+                 "attention, tcgen05 prefill) runs on this library's kernels",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_prefill(args):
     """``--workload prefill32k_chunk2048_bf16``: the chunked-prefill measurement as
     its own line (1 GPU; the reference arm has no GPU counterpart)."""
@@ -681,7 +751,7 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + [PREFILL_WORKLOAD], default="decode128k_bf16")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + [PREFILL_WORKLOAD, MODEL_WORKLOAD], default="decode128k_bf16")
     ap.add_argument("--calls-per-step", type=int, default=200)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true")
@@ -693,6 +763,8 @@ def main() -> int:
         args.warmup = 3
     if args.workload == PREFILL_WORKLOAD:
         return run_prefill(args)
+    if args.workload == MODEL_WORKLOAD:
+        return run_model(args)
     w = WORKLOADS[args.workload]
     if args.impl == "reference":
         return run_reference(args, w)

@@ -85,16 +85,19 @@ class RFSNModel:
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.dtype = resolve_dtype(config.model_dtype)
         self.params: Dict[str, torch.Tensor] = {}
-        gen = torch.Generator(device="cpu")
+        # random init normal(0, 0.02) drawn on the model's device (an 8B-parameter
+        # model initialises in seconds); norms start at ones / zeros
+        gen = torch.Generator(device=self.device)
         gen.manual_seed(0 if seed is None else seed)
         for name, shape in self.parameter_shapes().items():
             if name.endswith("norm.weight"):
-                t = torch.ones(shape)
+                t = torch.ones(shape, device=self.device, dtype=self.dtype)
             elif name == "norm.bias":
-                t = torch.zeros(shape)
+                t = torch.zeros(shape, device=self.device, dtype=self.dtype)
             else:
-                t = torch.empty(shape).normal_(0.0, 0.02, generator=gen)
-            self.params[name] = t.to(device=self.device, dtype=self.dtype)
+                t = torch.empty(shape, device=self.device, dtype=torch.float32).normal_(0.0, 0.02, generator=gen)
+                t = t.to(self.dtype)
+            self.params[name] = t
         self.layers = [RFSNLayer(config, i, self.params) for i in range(config.num_layers)]
 
     # ------------------------------------------------------------------ parameters

@@ -1,0 +1,55 @@
+"""Bench helpers and CLI (drop-in for rfsn_v10_5.bench / launcher bench)."""
+
+import pytest
+
+from rfsn_b200.__main__ import build_parser, config_from_args
+from rfsn_b200.bench import BenchResult
+
+
+def test_cli_defaults_match_reference_launcher():
+    a = build_parser().parse_args(["bench"])
+    # launcher.py:316-345 (model flags) and :370-377 (bench flags)
+    assert (a.hidden_dim, a.num_heads, a.num_kv_heads, a.head_dim, a.num_layers, a.vocab_size) == (512, 8, 0, 64, 4, 50000)
+    assert (a.hot_capacity, a.warm_capacity, a.cold_capacity, a.block_size_seq) == (512, 2048, 8192, 64)
+    assert (a.runtime_mode, a.model_dtype, a.rope_base, a.ffn_dim) == ("archived", "bfloat16", 10000.0, 0)
+    assert (a.prompt_len, a.decode_steps, a.warmup, a.repeats, a.seed_prompt_len, a.archive_seed_steps) == (256, 100, 2, 5, 8, 0)
+    cfg = config_from_args(a)
+    assert cfg.num_kv_heads == 8 and cfg.ffn_dim == 2048 and cfg.runtime_mode.value == "archived"
+
+
+def test_bench_result_string():
+    r = BenchResult("decode(steps=4)", 2.0, 1.5, 2.5, 2000.0, [1.5, 2.5])
+    assert str(r) == "decode(steps=4): mean=2.0ms  min=1.5ms  max=2.5ms  throughput=2000.0 tok/s"
+
+
+@pytest.mark.gpu
+def test_bench_prefill_and_decode_run_with_archiving_and_warmup(tmp_path):
+    from rfsn_b200.bench import bench_decode, bench_prefill
+    from rfsn_b200.cache import RFSNCache
+    from rfsn_b200.config import RFSNConfig
+    from rfsn_b200.model import RFSNModel
+
+    cfg = RFSNConfig(hidden_dim=256, num_heads=4, num_kv_heads=2, head_dim=64, num_layers=2, vocab_size=512,
+                     hot_capacity=16, block_size_seq=8, warm_capacity=64, cold_capacity=128, model_dtype="float32",
+                     disk_cache_dir=str(tmp_path))
+    model = RFSNModel(cfg, device="cuda", seed=1)
+    cache = RFSNCache(cfg, batch_size=1, device="cuda")
+    p = bench_prefill(model, cache, prompt_len=12, warmup=2, repeats=2)
+    assert p.name == "prefill(len=12)" and len(p.raw_ms) == 2 and p.throughput > 0
+    # warmup >= 2 raised in the reference (same position reused); here it runs
+    d = bench_decode(model, cache, steps=6, warmup=3, repeats=2, seed_prompt_len=8, archive_seed_steps=20)
+    assert d.name == "decode(steps=6)" and len(d.raw_ms) == 2 and d.throughput > 0
+    assert cache.layer(0).hot_seq_len == 0  # reset at the end, like the reference
+
+
+@pytest.mark.gpu
+def test_cli_bench_runs(tmp_path, capsys):
+    from rfsn_b200.__main__ import main
+
+    main(["bench", "--hidden-dim", "128", "--num-heads", "2", "--head-dim", "64", "--num-layers", "1",
+          "--vocab-size", "128", "--hot-capacity", "8", "--warm-capacity", "16", "--cold-capacity", "64",
+          "--block-size-seq", "4", "--model-dtype", "float32", "--disk-cache-dir", str(tmp_path),
+          "--prompt-len", "8", "--decode-steps", "5", "--warmup", "2", "--repeats", "2", "--archive-seed-steps", "9"])
+    out = capsys.readouterr().out.splitlines()
+    assert out[0].startswith("[bench] Model: 1L x 128d, 2H/2KVH, dtype=float32, runtime_mode=archived")
+    assert out[1].startswith("prefill(len=8): mean=") and out[2].startswith("decode(steps=5): mean=")
