@@ -657,6 +657,97 @@ def prefill_32k(args, device):
     }
 
 
+WARM_WORKLOAD = "warm_reload_bf16"
+WARM_DESC = ("one layer, 32 q / 8 kv heads, head_dim 128, bf16; a 32,768-token context appended in chunks of 2,048 "
+             "(hot ring 4,096, blocks of 2,048) with warm capacity 14,336 tokens, so half the archived blocks are "
+             "cold; each decode step then reloads every cold block (the reference's policy) and demotes others")
+
+
+def run_warm(args):
+    """``--workload warm_reload_bf16``: decode steps whose attention needs cold
+    blocks back in HBM. Disk path (npz read, checksum, decompress; demotions
+    write npz) vs. the pinned host tier (reloads stream from pinned host memory
+    on the side stream); residency decisions and metrics must be identical."""
+    import torch
+
+    from rfsn_b200.cache import LayerKVCache, paged_attention
+    from rfsn_b200.config import RFSNConfig, RuntimeMode
+
+    if args.impl == "reference":
+        print(json.dumps({"impl": "reference", "unavailable": "GPU-only workload; the reference CPU arm times the "
+                          "decode-attention workloads"}), flush=True)
+        return 0
+    torch.cuda.set_device(0)
+    device = torch.device("cuda", 0)
+    H, Hkv, D = 32, 8, 128
+    results, metrics = {}, {}
+    for mode, steps in (("disk", 1), ("host_tier", 32)):
+        with tempfile.TemporaryDirectory() as tmp:
+            cfg = RFSNConfig(hidden_dim=H * D, num_heads=H, num_kv_heads=Hkv, head_dim=D, num_layers=1,
+                             hot_capacity=4096, block_size_seq=2048, warm_capacity=14336, cold_capacity=65536,
+                             model_dtype="bfloat16", runtime_mode=RuntimeMode.ARCHIVED, disk_cache_dir=tmp,
+                             session_id="warm")
+            cache = LayerKVCache(cfg, 1, H, Hkv, layer_id=0, session_id="warm", device=device,
+                                 host_tier=(mode == "host_tier"))
+            gen = torch.Generator(device=device).manual_seed(5)
+            for a in range(0, 32768, 2048):
+                k = torch.randn((1, Hkv, 2048, D), generator=gen, device=device).to(torch.bfloat16)
+                v = torch.randn((1, Hkv, 2048, D), generator=gen, device=device).to(torch.bfloat16)
+                cache.evict_for_append(2048)
+                cache.append_exact(k, v)
+            torch.cuda.synchronize()
+            pos = 32768
+            times = []
+            for i in range(steps + 1):
+                q = torch.randn((1, H, 1, D), generator=gen, device=device)
+                k = torch.randn((1, Hkv, 1, D), generator=gen, device=device)
+                v = torch.randn((1, Hkv, 1, D), generator=gen, device=device)
+                t0 = time.perf_counter()
+                # attention_step with the decode prefetch awaited right after it is
+                # scheduled: residency decisions then do not depend on load speed
+                cache.evict_for_append(1)
+                q_rot = cache.append_rope(q, k, v, pos)
+                cache.maybe_prefetch_for_decode(pos)
+                cache.residency_manager.wait_for_prefetches(cache, timeout=120.0)
+                paged_attention(cache, q_rot, pos, cache.get_attention_segments())
+                torch.cuda.synchronize()
+                if i > 0:  # the first step also seals the full ring into a new block
+                    times.append(time.perf_counter() - t0)
+                pos += 1
+                if i == 1:  # after 2 steps: the counters the disk run ends with
+                    metrics[mode + "_after_2_steps"] = dict(cache.residency_manager.get_metrics())
+            m = cache.residency_manager.get_metrics()
+            metrics[mode] = {"steps": steps + 1, **m}
+            entry = {"steps_timed": steps, "ms_per_step": 1e3 * statistics.median(times),
+                     "blocks": sum(1 for _ in cache.block_manager.iter_blocks(layer_id=0)),
+                     "sync_loads_per_step": m["sync_loads"] / (steps + 1)}
+            if mode == "host_tier":
+                # H2D bandwidth of one reload: a held block copied pinned -> HBM on the side stream
+                bid, (kp, vp) = next(iter(cache._host_tier.items()))
+                n = kp.shape[1]
+                row = cache._allocate_rows(n)
+                cache._ops.upload(row, n, kp, vp)
+                torch.cuda.synchronize()
+                t0 = time.perf_counter()
+                reps = 20
+                for _ in range(reps):
+                    cache._ops.upload(row, n, kp, vp)
+                torch.cuda.synchronize()
+                dt = (time.perf_counter() - t0) / reps
+                entry["h2d_gbs"] = 2 * kp.numel() * kp.element_size() / dt / 1e9
+                entry["block_bytes"] = 2 * kp.numel() * kp.element_size()
+            results[mode] = entry
+    # identical residency decisions: the counters after the same 2 steps
+    same = metrics["disk_after_2_steps"] == metrics["host_tier_after_2_steps"]
+    line = {"metric": "decode step latency with cold-block reloads (ms, one layer)", "workload": WARM_WORKLOAD,
+            "desc": WARM_DESC, "n_gpus": 1, "dtype": "bf16", "higher_is_better": False,
+            "data": "synthetic N(0,1) K/V (seeded)", "value": results["host_tier"]["ms_per_step"], "unit": "ms/step",
+            "host_tier": results["host_tier"], "disk": results["disk"], "per_step_policy_equal": same,
+            "metrics": metrics}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 MODEL_WORKLOAD = "model8b_e2e_bf16"
 MODEL_DESC = ("Llama-3-8B-shaped model, random init normal(0, 0.02) seed 4: 32 layers, hidden 4096, 32 q / 8 kv "
               "heads, head_dim 128, SwiGLU FFN 14336, vocab 128256, RoPE theta 500000, bf16; 4,096-token prompt of "
@@ -751,7 +842,7 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + [PREFILL_WORKLOAD, MODEL_WORKLOAD], default="decode128k_bf16")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + [PREFILL_WORKLOAD, MODEL_WORKLOAD, WARM_WORKLOAD], default="decode128k_bf16")
     ap.add_argument("--calls-per-step", type=int, default=200)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true")
@@ -765,6 +856,8 @@ def main() -> int:
         return run_prefill(args)
     if args.workload == MODEL_WORKLOAD:
         return run_model(args)
+    if args.workload == WARM_WORKLOAD:
+        return run_warm(args)
     w = WORKLOADS[args.workload]
     if args.impl == "reference":
         return run_reference(args, w)

@@ -189,9 +189,23 @@ class DeviceOps:
         torch.cuda.current_stream().synchronize()
         return k_host.to(out_dtype), v_host.to(out_dtype)
 
+    def download_pinned(self, row: int, n: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """Arena rows -> pinned host tensors in the arena dtype (no conversion)."""
+        a = self.arena
+        k_host = torch.empty((a.groups, n, a.head_dim), dtype=a.dtype, pin_memory=True)
+        v_host = torch.empty_like(k_host, pin_memory=True)
+        native.check(
+            native.lib().rfsn_block_download(a.handle, row, n, k_host.data_ptr(), v_host.data_ptr(),
+                                             native.stream_ptr(), None),
+            "rfsn_block_download",
+        )
+        torch.cuda.current_stream().synchronize()
+        return k_host, v_host
+
     def upload(self, row: int, n: int, k_host: torch.Tensor, v_host: torch.Tensor) -> None:
         """Host -> arena copy on a side stream from pinned memory; the current
-        (compute) stream waits on the copy's event before later kernels."""
+        (compute) stream waits on the copy's event before later kernels. Tensors
+        already pinned, contiguous and in the arena dtype are copied as they are."""
         k = k_host.to(self.arena.dtype).contiguous().pin_memory()
         v = v_host.to(self.arena.dtype).contiguous().pin_memory()
         if self._upload_stream is None:
@@ -268,6 +282,7 @@ class LayerKVCache:
         device: Optional[torch.device | str] = None,
         pool_tokens: Optional[int] = None,
         ops: Optional[Any] = None,
+        host_tier: bool = False,
     ) -> None:
         self.config = config
         self.batch_size = batch_size
@@ -296,6 +311,11 @@ class LayerKVCache:
         self.storage = BlockStorage(Path(config.disk_cache_dir) / self.model_id / self.session_id / f"layer_{layer_id}")
         self.residency_manager = ResidencyManager(prefetch_margin_tokens=max(1, config.block_size_seq // 2))
         self._resident_rows: dict[BlockId, int] = {}
+        # Pinned host copies of demoted blocks (arena dtype), when enabled: the
+        # warm/cold policy and the npz persistence are unchanged, but a reload
+        # streams the block from pinned host memory on the side stream instead of
+        # reading, verifying and decompressing the npz file.
+        self._host_tier: Optional[dict[BlockId, tuple[torch.Tensor, torch.Tensor]]] = {} if host_tier else None
         self._deferred_free: list[tuple[int, int]] = []
         self._block_serial = 0
 
@@ -375,6 +395,8 @@ class LayerKVCache:
         self._arena_v.zero_()
         self._alloc.reset()
         self._resident_rows.clear()
+        if self._host_tier is not None:
+            self._host_tier.clear()
         self._deferred_free.clear()
         self._attended, self._attended_spans = [], []
         self._dirty = True
@@ -498,6 +520,29 @@ class LayerKVCache:
         if row is None:
             self.block_manager.mark_unmaterializable(manifest.block_id, reason="warm payload missing from resident set")
             return
+        if self._host_tier is not None:
+            n = manifest.token_count
+            if manifest.block_id in self._host_tier and manifest.checksum and manifest.payload_path \
+                    and Path(manifest.payload_path).exists():
+                # already persisted and held in pinned memory: the state change of
+                # persist_block without rewriting identical bytes
+                self._free_rows(row, n)
+                manifest.residency = BlockLocation.COLD_DISK
+                manifest.materializable = True
+                manifest.failure_reason = None
+                manifest.touch()
+                self.storage.write_manifest(manifest)
+                return
+            k_pin, v_pin = self._ops.download_pinned(row, n)
+            self._free_rows(row, n)
+            self._host_tier[manifest.block_id] = (k_pin, v_pin)
+            out = np.float16 if self.storage_array_dtype == np.float16 else np.float32
+            shape = (self.batch_size, self.num_kv_heads, n, self.config.head_dim)
+            payload = {"keys": k_pin.to(torch.float32).numpy().astype(out).reshape(shape),
+                       "values": v_pin.to(torch.float32).numpy().astype(out).reshape(shape)}
+            manifest.dtype = payload["keys"].dtype.name
+            self.storage.persist_block(manifest, payload)
+            return
         payload = self._download_block(row, manifest.token_count)
         self._free_rows(row, manifest.token_count)
         manifest.dtype = payload["keys"].dtype.name
@@ -513,14 +558,22 @@ class LayerKVCache:
         return manifest.block_id in self._resident_rows
 
     def load_manifest_payload_only(self, manifest: BlockManifest) -> Optional[dict[str, np.ndarray]]:
+        if self._host_tier is not None:
+            held = self._host_tier.get(manifest.block_id)
+            if held is not None:
+                return {"keys": held[0], "values": held[1]}  # pinned tensors, arena dtype
         return self.storage.load_block(manifest)
 
     def promote_manifest_from_payload(self, manifest: BlockManifest, payload: dict[str, np.ndarray]) -> None:
         """cache.py:309-319: the payload is uploaded into fresh pool rows."""
         n = manifest.token_count
         groups, D = self.batch_size * self.num_kv_heads, self.config.head_dim
-        k = torch.as_tensor(np.asarray(payload["keys"])).reshape(groups, n, D)
-        v = torch.as_tensor(np.asarray(payload["values"])).reshape(groups, n, D)
+        keys, values = payload["keys"], payload["values"]
+        if isinstance(keys, torch.Tensor):
+            k, v = keys.reshape(groups, n, D), values.reshape(groups, n, D)
+        else:
+            k = torch.as_tensor(np.asarray(keys)).reshape(groups, n, D)
+            v = torch.as_tensor(np.asarray(values)).reshape(groups, n, D)
         row = self._allocate_rows(n)
         self._ops.upload(row, n, k, v)
         self._resident_rows[manifest.block_id] = row
@@ -845,6 +898,7 @@ class RFSNCache:
         device: Optional[torch.device | str] = None,
         pool_tokens: Optional[int] = None,
         ops_factory: Optional[Any] = None,
+        host_tier: bool = False,
     ) -> None:
         self.config = config
         self.model_id = model_id or derive_model_id(config)
@@ -861,6 +915,7 @@ class RFSNCache:
                 device=device,
                 pool_tokens=pool_tokens,
                 ops=ops_factory() if ops_factory is not None else None,
+                host_tier=host_tier,
             )
             for i in range(config.num_layers)
         ]

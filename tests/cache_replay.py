@@ -78,13 +78,13 @@ def replay_ring(name, ops_factory):
         return cache
 
 
-def replay_residency(name, ops_factory):
+def replay_residency(name, ops_factory, host_tier=False):
     from rfsn_b200 import LayerKVCache
 
     sc = RESIDENCY[name]
     with tempfile.TemporaryDirectory() as tmp:
         cfg = _config(sc["hot_capacity"], sc["block_size"], "archived", sc["warm_capacity"], tmp)
-        cache = LayerKVCache(cfg, 1, 2, 1, layer_id=0, session_id="golden", ops=ops_factory())
+        cache = LayerKVCache(cfg, 1, 2, 1, layer_id=0, session_id="golden", ops=ops_factory(), host_tier=host_tier)
         pos = 0
         for step in sc["steps"]:
             n = step["incoming"]

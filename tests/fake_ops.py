@@ -56,6 +56,10 @@ class FakeDeviceOps:
         self.calls.append(("download", row, n))
         return self.k[:, row:row + n].to(out_dtype).clone(), self.v[:, row:row + n].to(out_dtype).clone()
 
+    def download_pinned(self, row, n):
+        self.calls.append(("download_pinned", row, n))
+        return self.k[:, row:row + n].clone(), self.v[:, row:row + n].clone()
+
     def upload(self, row, n, k_host, v_host):
         self.calls.append(("upload", row, n))
         self.k[:, row:row + n] = k_host.to(self.k.dtype)

@@ -21,9 +21,10 @@ def test_ring_trace_on_device(name):
     replay_ring(name, lambda: None)
 
 
+@pytest.mark.parametrize("host_tier", [False, True])
 @pytest.mark.parametrize("name", residency_names())
-def test_residency_trace_on_device(name):
-    replay_residency(name, lambda: None)
+def test_residency_trace_on_device(name, host_tier):
+    replay_residency(name, lambda: None, host_tier=host_tier)
 
 
 def _round(x, dtype):

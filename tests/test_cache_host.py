@@ -29,9 +29,12 @@ def test_ring_and_page_table_match_reference_trace(name):
     replay_ring(name, FakeDeviceOps)
 
 
+@pytest.mark.parametrize("host_tier", [False, True])
 @pytest.mark.parametrize("name", residency_names())
-def test_residency_matches_reference_trace(name):
-    replay_residency(name, FakeDeviceOps)
+def test_residency_matches_reference_trace(name, host_tier):
+    # the pinned host tier changes where a reloaded block's bytes come from,
+    # never the warm/cold decisions, metrics or attended values
+    replay_residency(name, FakeDeviceOps, host_tier=host_tier)
 
 
 def test_device_page_table_records():
