@@ -173,10 +173,17 @@ def load_library() -> ctypes.CDLL:
     return lib
 
 
+_device_seen = False
+
+
 def lib() -> ctypes.CDLL:
+    """The loaded library, after checking (once per process) that a CUDA device is visible."""
+    global _device_seen
     lib_ = load_library()
-    if not torch.cuda.is_available():
-        raise NativeUnavailable("the B200 attention path needs a CUDA device; none is visible")
+    if not _device_seen:
+        if not torch.cuda.is_available():
+            raise NativeUnavailable("the B200 attention path needs a CUDA device; none is visible")
+        _device_seen = True
     return lib_
 
 
@@ -202,9 +209,18 @@ def check(status: int, what: str) -> None:
     raise RuntimeError(f"{what}: {msg}")
 
 
+_raw_current_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+_current_device = getattr(torch._C, "_cuda_getDevice", None)
+
+
 def stream_ptr(stream: Optional[torch.cuda.Stream] = None) -> int:
-    s = stream if stream is not None else torch.cuda.current_stream()
-    return int(s.cuda_stream)
+    """cudaStream_t of ``stream``, else of the current stream of the current
+    device (one call into torch's C layer: this runs on every decode step)."""
+    if stream is not None:
+        return int(stream.cuda_stream)
+    if _raw_current_stream is not None and _current_device is not None:
+        return int(_raw_current_stream(_current_device()))
+    return int(torch.cuda.current_stream().cuda_stream)
 
 
 def dtype_code(dtype: torch.dtype) -> int:

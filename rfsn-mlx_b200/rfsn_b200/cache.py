@@ -121,6 +121,14 @@ class _RowAllocator:
         self.free = [[self.start, self.end]]
 
 
+def _as(x: torch.Tensor, device: torch.device, dtype: torch.dtype) -> torch.Tensor:
+    """x on ``device`` in ``dtype``, contiguous; returned as is when it already is
+    (the per-call conversions of the decode path are mostly no-ops)."""
+    if x.dtype == dtype and x.device == device and x.is_contiguous():
+        return x
+    return x.to(device=device, dtype=dtype).contiguous()
+
+
 class DeviceOps:
     """Device mechanics of one layer cache: arena allocation, ring writes,
     seal copies, block transfers and the page-table upload. Every method is a
@@ -557,6 +565,11 @@ class LayerKVCache:
     def is_manifest_resident(self, manifest: BlockManifest) -> bool:
         return manifest.block_id in self._resident_rows
 
+    def all_blocks_resident(self) -> bool:
+        """Every live block of this layer has rows in the arena (the resident set
+        only ever holds live blocks, so equal sizes mean no cold block)."""
+        return len(self._resident_rows) == len(self.block_manager.page_table.layer_entries(self.layer_id))
+
     def load_manifest_payload_only(self, manifest: BlockManifest) -> Optional[dict[str, np.ndarray]]:
         if self._host_tier is not None:
             held = self._host_tier.get(manifest.block_id)
@@ -610,7 +623,7 @@ class LayerKVCache:
     def _kv_arg(self, x: torch.Tensor) -> torch.Tensor:
         if x.dim() != 4 or x.shape[0] != self.batch_size or x.shape[1] != self.num_kv_heads:
             raise ValueError(f"expected K/V shaped [{self.batch_size}, {self.num_kv_heads}, L, {self.config.head_dim}]")
-        return x.to(device=self.device, dtype=self.dtype).contiguous()
+        return _as(x, self.device, self.dtype)
 
     def append_exact(self, k: torch.Tensor, v: torch.Tensor) -> None:
         """cache.py:341-361: write already-rotated K and V into the ring."""
@@ -639,7 +652,7 @@ class LayerKVCache:
         """
         seq_len = int(k.shape[2])
         self._check_append(seq_len)
-        qc = q.to(device=self.device, dtype=self.dtype).contiguous()
+        qc = _as(q, self.device, self.dtype)
         kc, vc = self._kv_arg(k), self._kv_arg(v)
         q_out = self._ops.append(qc, kc, vc, self.inv_freq(), int(start_pos), self.config.hot_capacity,
                                  self.hot_write_index)
@@ -841,7 +854,7 @@ def paged_attention(cache: LayerKVCache, q: torch.Tensor, q_start_pos: int, segm
         raise RuntimeError("run_segmented_attention requires at least one KV segment")
     if q.dim() != 4 or q.shape[0] != cache.batch_size or q.shape[3] != cache.config.head_dim:
         raise ValueError(f"q must be [batch={cache.batch_size}, heads, q_len, head_dim={cache.config.head_dim}]")
-    qf = q.to(device=cache.device, dtype=torch.float32).contiguous()
+    qf = _as(q, cache.device, torch.float32)
     B, H, Lq, D = (int(x) for x in qf.shape)
     out = torch.empty((B, H, Lq, D), dtype=torch.float32, device=cache.device)
     lse = torch.empty((B, H, Lq), dtype=torch.float32, device=cache.device) if want_lse else None

@@ -17,7 +17,8 @@ caller drains it, the payload is staged in pinned host memory and copied into
 the device arena with an asynchronous host-to-device copy on a side stream;
 the compute stream waits on that copy's event before its next kernel.
 One exact shortcut: a decode-step prefetch check on a layer without any cold
-block returns at once (both candidate rules need a cold block).
+block returns at once (both candidate rules need a cold block); when every
+live block is resident in HBM that is known without a scan.
 """
 
 from __future__ import annotations
@@ -91,6 +92,10 @@ class ResidencyManager:
         self.drain_completed_prefetches(cache)
         live = cache.block_manager.page_table.layer_entries(cache.layer_id)
         # Both candidate rules need a cold block; with none, nothing can be scheduled.
+        # O(1) when every live block is resident in HBM, else a scan.
+        all_resident = getattr(cache, "all_blocks_resident", None)
+        if all_resident is not None and all_resident():
+            return
         if not any(m.residency == BlockLocation.COLD_DISK for m in live):
             return
         manifests = [m for m in live if m.materializable]
