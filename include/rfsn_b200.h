@@ -93,8 +93,21 @@ typedef struct rfsn_hot_window {
     int32_t head_index;   /* hot_head_index */
     int32_t length;       /* hot_seq_len */
     int32_t start_pos;    /* hot_start */
-    int32_t reserved[3];
+    int32_t reserved;
+    /* Optional device int32[RFSN_STEP_STATE_LEN] read by the kernel when it
+     * runs (so one captured CUDA graph serves every decode step): the query
+     * position replaces q_pos0 and the hot window replaces head_index / length
+     * / start_pos. NULL: the fields above are used. See RFSN_STEP_*. */
+    const int32_t* step_state;
 } rfsn_hot_window;
+
+/* Layout of a device step state (int32). */
+#define RFSN_STEP_POS 0          /* absolute position of the first new token */
+#define RFSN_STEP_WRITE_INDEX 1  /* ring slot the new tokens are written to */
+#define RFSN_STEP_HEAD 2         /* hot_head_index after the append */
+#define RFSN_STEP_LENGTH 3       /* hot_seq_len after the append */
+#define RFSN_STEP_START 4        /* hot_start after the append */
+#define RFSN_STEP_STATE_LEN 8
 
 /* One K/V arena pair of a layer; holds the TMA descriptors the decode kernel
  * streams tiles with. Created once per cache layer. */
@@ -134,6 +147,16 @@ RFSN_API rfsn_status rfsn_rope_append(const void* q, const void* k, const void* 
                              float* q_out,
                              const rfsn_arena* arena, int ring_row0, int capacity, int write_index,
                              void* stream);
+
+/* rfsn_rope_append with the position and ring write index read on the device
+ * from step_state[RFSN_STEP_POS] and step_state[RFSN_STEP_WRITE_INDEX] when the
+ * kernel runs (capturable once in a CUDA graph and replayed for every decode
+ * step). No counterpart in the reference: it only moves two arguments of
+ * layer.py:131-135 into device memory. */
+RFSN_API rfsn_status rfsn_rope_append_step(const void* q, const void* k, const void* v, int in_dtype,
+                                           const float* inv_freq, const int32_t* step_state, int batch, int q_heads,
+                                           int kv_heads, int len, int head_dim, float* q_out,
+                                           const rfsn_arena* arena, int ring_row0, int capacity, void* stream);
 
 /* ------------------------------------------------------------------------
  * Copy rows inside an arena (both K and V, every batch*kv head).

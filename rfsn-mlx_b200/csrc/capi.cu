@@ -213,6 +213,30 @@ rfsn_status rfsn_rope_append(const void* q, const void* k, const void* v, int in
                               arena->v, arena->rows, ring_row0, capacity, write_index, static_cast<cudaStream_t>(stream));
 }
 
+rfsn_status rfsn_rope_append_step(const void* q, const void* k, const void* v, int in_dtype, const float* inv_freq,
+                                  const int32_t* step_state, int batch, int q_heads, int kv_heads, int len,
+                                  int head_dim, float* q_out, const rfsn_arena* arena, int ring_row0, int capacity,
+                                  void* stream) {
+    RFSN_CHECK_ARG(step_state != nullptr, "rfsn_rope_append_step: NULL step state");
+    RFSN_CHECK_ARG(arena != nullptr, "rfsn_rope_append_step: NULL arena");
+    RFSN_CHECK_ARG(k != nullptr && v != nullptr, "rfsn_rope_append_step: k and v are required");
+    RFSN_CHECK_ARG(valid_dtype(in_dtype) && in_dtype == arena->dtype,
+                   "rfsn_rope_append_step: input dtype %d differs from cache dtype %d", in_dtype, arena->dtype);
+    RFSN_CHECK_ARG(batch > 0 && kv_heads > 0 && len > 0 && q_heads >= 0, "rfsn_rope_append_step: non-positive shape");
+    RFSN_CHECK_ARG(head_dim == arena->head_dim && batch * kv_heads == arena->groups,
+                   "rfsn_rope_append_step: shape does not match the arena");
+    RFSN_CHECK_ARG(capacity > 0 && ring_row0 >= 0 && ring_row0 + capacity <= arena->rows,
+                   "rfsn_rope_append_step: ring rows outside the arena");
+    if (len > capacity) {
+        set_error("append_exact: chunk of %d tokens exceeds the ring capacity %d", len, capacity);
+        return RFSN_ERR_OVERFLOW;
+    }
+    const int qh = (inv_freq != nullptr && q != nullptr) ? q_heads : 0;
+    return rope_append_launch(in_dtype, q, k, v, inv_freq, 0, batch, qh, kv_heads, len, head_dim, q_out, arena->k,
+                              arena->v, arena->rows, ring_row0, capacity, 0, static_cast<cudaStream_t>(stream),
+                              step_state);
+}
+
 rfsn_status rfsn_arena_copy_rows(const rfsn_arena* arena, int src_row0, int src_offset, int src_wrap, int dst_row0,
                                  int count, void* stream) {
     RFSN_CHECK_ARG(arena != nullptr, "rfsn_arena_copy_rows: NULL arena");
@@ -390,8 +414,15 @@ rfsn_status rfsn::paged_attention_impl(const rfsn_arena* arena, const float* q, 
     const int sms = sm_count_cached();
     const bool use_fast = arena->has_tma && arena->head_dim == 128 && a.nslots <= 4;
     // chunked prefill on the tensor cores: float4 q/out rows need 16-byte alignment
-    const bool use_prefill = peer == nullptr && arena->has_tma && arena->head_dim == 128 && q_len >= kPrefillMinRows &&
-                             a.G <= 128 && (uintptr_t)q % 16 == 0 && (uintptr_t)out % 16 == 0;
+    const bool stepped = hot->step_state != nullptr;  // position / hot window read on the device
+    const bool use_prefill = !stepped && peer == nullptr && arena->has_tma && arena->head_dim == 128 &&
+                             q_len >= kPrefillMinRows && a.G <= 128 && (uintptr_t)q % 16 == 0 &&
+                             (uintptr_t)out % 16 == 0;
+    if (stepped && !use_fast) {
+        set_error("a device step state needs the tensor-core decode shape (bf16/f16, head_dim 128, <= 4 query "
+                  "slots per KV head)");
+        return RFSN_ERR_UNSUPPORTED;
+    }
     if (use_prefill) {
         const WsLayout w = ws_layout(a.groups, 1, 1, a.slots_ws, 128);
         if (w.total > workspace_bytes) {
@@ -430,7 +461,11 @@ rfsn_status rfsn::paged_attention_impl(const rfsn_arena* arena, const float* q, 
         fast::Params p;
         int splits, tps;
         const int cap = max_splits > 0 ? (max_splits < fast_max_splits() ? max_splits : fast_max_splits()) : fast_max_splits();
-        choose_splits(total_tiles, a.groups, sms * kFastCtasPerSm, cap, &splits, &tps);
+        // With a device step state the hot window is only known when the kernel
+        // runs: the split count is chosen for the largest window the ring holds
+        // (two pieces), and the kernel derives its tile ranges itself.
+        const int plan_tiles = stepped ? table->archived_tiles + (hot->capacity + kTile - 1) / kTile + 1 : total_tiles;
+        choose_splits(plan_tiles, a.groups, sms * kFastCtasPerSm, cap, &splits, &tps);
         const WsLayout w = ws_layout(a.groups, 1, splits, a.slots_ws, 128);
         if (w.total > workspace_bytes) {
             set_error("attention workspace too small: need %zu bytes, have %zu", w.total, workspace_bytes);
@@ -463,6 +498,7 @@ rfsn_status rfsn::paged_attention_impl(const rfsn_arena* arena, const float* q, 
         p.ws = ws_view(workspace, w);
         memset(&p.peer, 0, sizeof(p.peer));
         if (peer != nullptr) p.peer = *peer;
+        p.dyn = hot->step_state;
         return fast_launch(arena->dtype, arena->maps, p, kFastStages, s);
     }
     generic::Params p;

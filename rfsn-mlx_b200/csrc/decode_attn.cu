@@ -64,8 +64,30 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int split = blockIdx.x, bh = blockIdx.y;
-    const int tile0 = split * p.tiles_per_split;
-    const int ntiles = min(p.tiles_per_split, p.total_tiles - tile0);
+    // Query position and hot window: launch arguments, or a device step state
+    // (RFSN_STEP_*) read when the kernel runs. The state may be written by the
+    // work this launch overlaps, so it is read after the dependency wait; the
+    // tile ranges follow from it (the split count was fixed on the host for the
+    // largest window).
+    int q_pos0 = p.q_pos0, head = p.head, hlen = p.hlen, hstart = p.hstart;
+    int total_tiles = p.total_tiles, tiles_per_split = p.tiles_per_split;
+    if (p.dyn != nullptr) {
+        griddep_wait();
+        q_pos0 = p.dyn[0];
+        head = p.dyn[2];
+        hlen = p.dyn[3];
+        hstart = p.dyn[4];
+        if (head < 0 || head >= p.capacity || hlen < 0 || hlen > p.capacity) {  // malformed: attend to no hot key
+            if (threadIdx.x == 0 && split == 0 && bh == 0) atomicExch(p.ws.error, kDevErrBadTable);
+            head = 0;
+            hlen = 0;
+        }
+        const int first = min(hlen, p.capacity - head);
+        total_tiles = p.archived_tiles + (first + kTile - 1) / kTile + (hlen - first + kTile - 1) / kTile;
+        tiles_per_split = (total_tiles + p.splits - 1) / p.splits;
+    }
+    const int tile0 = split * tiles_per_split;
+    const int ntiles = min(tiles_per_split, total_tiles - tile0);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -90,7 +112,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
             cur.records = p.records;
             cur.n_blocks = p.n_blocks;
             cur.archived_tiles = p.archived_tiles;
-            cur.init_hot(p.ring_row0, p.capacity, p.head, p.hlen, p.hstart);
+            cur.init_hot(p.ring_row0, p.capacity, head, hlen, hstart);
             cur.seek_warp(tile0);
         }
         if (lane == 0 && ntiles > 0) {
@@ -173,8 +195,8 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
             }
         }
     }
-    const int qp0 = p.q_pos0 + sl0 / p.groups_per_kv;
-    const int qp1 = p.q_pos0 + (sl0 + 1) / p.groups_per_kv;
+    const int qp0 = q_pos0 + sl0 / p.groups_per_kv;
+    const int qp1 = q_pos0 + (sl0 + 1) / p.groups_per_kv;
 
     float acc[8][4];
 #pragma unroll

@@ -15,7 +15,13 @@ template <typename TIn, typename TCache>
 __global__ void rope_append_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k, const TIn* __restrict__ v,
                                    const float* __restrict__ inv_freq, int pos0, int batch, int q_heads, int kv_heads,
                                    int len, int head_dim, float* __restrict__ q_out, TCache* __restrict__ ak,
-                                   TCache* __restrict__ av, int rows, int ring_row0, int capacity, int write_index) {
+                                   TCache* __restrict__ av, int rows, int ring_row0, int capacity, int write_index,
+                                   const int* __restrict__ step_state) {
+    if (step_state != nullptr) {  // position and write slot chosen when the kernel runs
+        pos0 = step_state[0];
+        write_index = step_state[1];
+        if ((unsigned)write_index >= (unsigned)capacity) return;  // never write outside the ring
+    }
     const int half = head_dim >> 1;
     const long q_rows = (long)batch * q_heads * len;
     const long kv_rows = (long)batch * kv_heads * len;
@@ -84,7 +90,8 @@ __global__ void copy_rows_kernel(uint8_t* __restrict__ ak, uint8_t* __restrict__
 
 rfsn_status rope_append_launch(int dtype, const void* q, const void* k, const void* v, const float* inv_freq, int pos0,
                                int batch, int q_heads, int kv_heads, int len, int head_dim, float* q_out, void* ak,
-                               void* av, int rows, int ring_row0, int capacity, int write_index, cudaStream_t stream) {
+                               void* av, int rows, int ring_row0, int capacity, int write_index, cudaStream_t stream,
+                               const int* step_state) {
     const long total = ((long)batch * (q_heads + kv_heads) * len) * (head_dim / 2);
     const int threads = 256;
     long blocks = (total + threads - 1) / threads;
@@ -94,7 +101,7 @@ rfsn_status rope_append_launch(int dtype, const void* q, const void* k, const vo
     ring::rope_append_kernel<T, T><<<(unsigned)blocks, threads, 0, stream>>>(                                   \
         static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(v), inv_freq, pos0, batch,    \
         q_heads, kv_heads, len, head_dim, q_out, static_cast<T*>(ak), static_cast<T*>(av), rows, ring_row0,     \
-        capacity, write_index)
+        capacity, write_index, step_state)
     if (dtype == RFSN_F32) {
         RFSN_ROPE_LAUNCH(float);
     } else if (dtype == RFSN_F16) {

@@ -46,6 +46,7 @@ EXPORTED_SYMBOLS = (
     "rfsn_arena_create",
     "rfsn_arena_destroy",
     "rfsn_rope_append",
+    "rfsn_rope_append_step",
     "rfsn_arena_copy_rows",
     "rfsn_block_upload",
     "rfsn_block_download",
@@ -87,8 +88,13 @@ class HotWindowC(ctypes.Structure):
         ("head_index", ctypes.c_int32),
         ("length", ctypes.c_int32),
         ("start_pos", ctypes.c_int32),
-        ("reserved", ctypes.c_int32 * 3),
+        ("reserved", ctypes.c_int32),
+        ("step_state", ctypes.c_void_p),  # optional device int32[8] (RFSN_STEP_*), read when the kernel runs
     ]
+
+
+# Device step state layout (int32 indices), include/rfsn_b200.h RFSN_STEP_*
+STEP_POS, STEP_WRITE_INDEX, STEP_HEAD, STEP_LENGTH, STEP_START, STEP_STATE_LEN = 0, 1, 2, 3, 4, 8
 
 
 class SegmentDescC(ctypes.Structure):
@@ -134,6 +140,7 @@ def load_library() -> ctypes.CDLL:
         "rfsn_arena_create": (i32, [vp, vp, i32, i32, i32, i32, ctypes.POINTER(vp)]),
         "rfsn_arena_destroy": (i32, [vp]),
         "rfsn_rope_append": (i32, [vp, vp, vp, i32, vp, i32, i32, i32, i32, i32, i32, vp, vp, i32, i32, i32, vp]),
+        "rfsn_rope_append_step": (i32, [vp, vp, vp, i32, vp, vp, i32, i32, i32, i32, i32, vp, vp, i32, i32, vp]),
         "rfsn_arena_copy_rows": (i32, [vp, i32, i32, i32, i32, i32, vp]),
         "rfsn_block_upload": (i32, [vp, i32, i32, vp, vp, vp, vp]),
         "rfsn_block_download": (i32, [vp, i32, i32, vp, vp, vp, vp]),

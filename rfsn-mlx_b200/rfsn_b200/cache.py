@@ -843,13 +843,18 @@ class LayerKVCache:
 
 def paged_attention(cache: LayerKVCache, q: torch.Tensor, q_start_pos: int, segments: PagedSegments,
                     *, want_lse: bool = False, max_splits: int = 0, workspace: Optional[native.Workspace] = None,
-                    peers: Optional[Any] = None):
+                    peers: Optional[Any] = None, step_state: Optional[torch.Tensor] = None):
     """Exact attention of q over a layer's page table + hot window.
 
     With ``peers`` (a ``sharded.PeerGroup``) the kernel also merges the
     results of every rank of the group over NVLink, so the returned output is
     the attention over the whole sharded context (an empty local shard is
-    allowed then)."""
+    allowed then).
+
+    With ``step_state`` (device int32[8], ``_native.STEP_*``) the query position
+    and the hot window are read from device memory when the kernel runs, so a
+    captured CUDA graph of the call stays valid while the ring advances (the
+    page table is still captured by value)."""
     if len(segments) == 0 and peers is None:
         raise RuntimeError("run_segmented_attention requires at least one KV segment")
     if q.dim() != 4 or q.shape[0] != cache.batch_size or q.shape[3] != cache.config.head_dim:
@@ -870,7 +875,8 @@ def paged_attention(cache: LayerKVCache, q: torch.Tensor, q_start_pos: int, segm
         if segments.n_archived != len(segments):
             # hot-only view taken without a snapshot: use the live ring state
             head, hlen, hstart = cache.hot_head_index, cache.hot_seq_len, cache.hot_start
-    hot = native.HotWindowC(0, cache.config.hot_capacity, head, hlen, hstart)
+    hot = native.HotWindowC(0, cache.config.hot_capacity, head, hlen, hstart, 0,
+                            step_state.data_ptr() if step_state is not None else None)
     ws = workspace if workspace is not None else native.default_workspace(cache.device)
     nbytes = native.workspace_bytes(B, H, cache.num_kv_heads, Lq, D, max_splits)
     buf = ws.get(nbytes)

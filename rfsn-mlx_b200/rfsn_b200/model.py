@@ -28,7 +28,8 @@ import numpy as np
 import torch
 import torch.nn.functional as F
 
-from .cache import RFSNCache
+from . import _native as native
+from .cache import RFSNCache, _as, paged_attention
 from .config import RFSNConfig, RuntimeMode, resolve_dtype
 from .layer import attention_step
 
@@ -58,7 +59,8 @@ class RFSNLayer:
     def _w(self, name: str) -> torch.Tensor:
         return self.p[f"layers.{self.layer_idx}.{name}"]
 
-    def __call__(self, x: torch.Tensor, layer_cache, start_pos: int) -> torch.Tensor:
+    def __call__(self, x: torch.Tensor, layer_cache, start_pos: int, attn=None) -> torch.Tensor:
+        """``attn(q, k, v)`` replaces the attention step (used by the captured decode graph)."""
         cfg = self.config
         B, L, _ = x.shape
         H, Hkv, D = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
@@ -67,8 +69,8 @@ class RFSNLayer:
         q = F.linear(xn, self._w("q_proj.weight")).reshape(B, L, H, D).transpose(1, 2)
         k = F.linear(xn, self._w("k_proj.weight")).reshape(B, L, Hkv, D).transpose(1, 2)
         v = F.linear(xn, self._w("v_proj.weight")).reshape(B, L, Hkv, D).transpose(1, 2)
-        attn = attention_step(q, k, v, layer_cache, start_pos)  # float32 [B, H, L, D]
-        attn = attn.transpose(1, 2).reshape(B, L, H * D).to(x.dtype)
+        a = attention_step(q, k, v, layer_cache, start_pos) if attn is None else attn(q, k, v)  # float32 [B, H, L, D]
+        attn = a.transpose(1, 2).reshape(B, L, H * D).to(x.dtype)
         x = residual + F.linear(attn, self._w("o_proj.weight"))
         h = _rms_norm(x, self._w("ffn_norm.weight"), cfg.norm_eps)
         ffn = F.linear(F.silu(F.linear(h, self._w("gate_proj.weight"))) * F.linear(h, self._w("up_proj.weight")),
@@ -99,6 +101,8 @@ class RFSNModel:
                 t = t.to(self.dtype)
             self.params[name] = t
         self.layers = [RFSNLayer(config, i, self.params) for i in range(config.num_layers)]
+        self.use_graphs = True
+        self._graph: Optional["_DecodeGraph"] = None
 
     # ------------------------------------------------------------------ parameters
     def parameter_shapes(self) -> Dict[str, Tuple[int, ...]]:
@@ -208,9 +212,20 @@ class RFSNModel:
         return out[0] if len(out) == 1 else torch.cat(out, dim=1)
 
     def decode_step(self, token_id: ArrayLike, cache: RFSNCache, pos: int) -> torch.Tensor:
-        """model.py:167-189: token_id (B,) -> logits (B, vocab)."""
+        """model.py:167-189: token_id (B,) -> logits (B, vocab).
+
+        When the cache allows it (bf16/f16, head_dim 128, <= 4 query heads per KV
+        head, every archived block resident in HBM, no prefetch in flight) the
+        step replays a CUDA graph of the whole network, captured once and again
+        after every page-table change; the host only runs the cache bookkeeping.
+        Otherwise (or with ``use_graphs = False``) it runs op by op."""
         self._validate_decode_bounds(cache, pos)
         token_id = torch.as_tensor(np.asarray(token_id)) if isinstance(token_id, np.ndarray) else token_id
+        if self.use_graphs:
+            if self._graph is None or self._graph.cache is not cache:
+                self._graph = _DecodeGraph(self, cache) if _DecodeGraph.supported(self, cache) else None
+            if self._graph is not None and self._graph.eligible():
+                return self._graph.step(token_id, pos)
         x = self._embed(token_id.reshape(-1, 1))
         return self._forward(x, cache, pos)[:, 0, :]
 
@@ -276,6 +291,132 @@ class RFSNModel:
             return torch.gather(sorted_idx, 1, local)[:, 0].to(torch.int32)
         probs = torch.softmax(scaled, dim=-1)
         return torch.multinomial(probs, 1, generator=generator)[:, 0].to(torch.int32)
+
+
+class _DecodeGraph:
+    """The decode step of a whole model as one CUDA graph.
+
+    Per step the host runs each layer's cache bookkeeping exactly as
+    ``attention_step`` would (seal rule, append counters, prefetch hook,
+    segment walk with its LRU touches) and writes the step state (position,
+    ring write index, hot window) to device memory; the graph then embeds the
+    token, runs every layer with the fused RoPE/append and the decode kernel
+    reading that state, and writes the logits. The page tables, arena
+    descriptors and workspace are captured by value, so the graph is captured
+    again whenever one of them changes (a seal, a promotion, an arena growth)."""
+
+    RING = 8  # pinned step-state buffers in flight
+
+    @staticmethod
+    def supported(model: "RFSNModel", cache: RFSNCache) -> bool:
+        cfg = model.config
+        return (model.device.type == "cuda" and model.dtype in (torch.bfloat16, torch.float16)
+                and cfg.head_dim == 128 and cfg.num_heads // cfg.num_kv_heads <= 4
+                and all(lc.dtype == model.dtype for lc in cache.layers))
+
+    def __init__(self, model: "RFSNModel", cache: RFSNCache) -> None:
+        self.model = model
+        self.cache = cache
+        dev = model.device
+        self.tok = torch.zeros((0,), dtype=torch.long, device=dev)
+        self.state_dev = torch.zeros(native.STEP_STATE_LEN, dtype=torch.int32, device=dev)
+        self.state_host = [torch.zeros(native.STEP_STATE_LEN, dtype=torch.int32).pin_memory() for _ in range(self.RING)]
+        self.state_done = [torch.cuda.Event() for _ in range(self.RING)]
+        self.n = 0
+        self.workspace = native.Workspace(dev)
+        self.graph: Optional[torch.cuda.CUDAGraph] = None
+        self.key = None
+        self.logits: Optional[torch.Tensor] = None
+        self.replays = 0
+        self.captures = 0
+
+    def eligible(self) -> bool:
+        layers = self.cache.layers
+        first = (layers[0].hot_head_index, layers[0].hot_seq_len, layers[0].hot_start)
+        for lc in layers:
+            if lc.residency_manager.has_pending or not lc.all_blocks_resident():
+                return False
+            if (lc.hot_head_index, lc.hot_seq_len, lc.hot_start) != first:
+                return False
+        return True
+
+    def step(self, token_id: torch.Tensor, pos: int) -> torch.Tensor:
+        model, cache = self.model, self.cache
+        segs, write_index = [], None
+        for lc in cache.layers:
+            # attention_step's host part for one token (layer.py:134-139)
+            lc.evict_for_append(1)
+            wi = lc.hot_write_index
+            lc._check_append(1)
+            lc.hot_seq_len += 1
+            lc.maybe_prefetch_for_decode(pos)
+            sg = lc.get_attention_segments()
+            segs.append(sg)
+            write_index = wi
+        head, hlen, hstart = segs[0].hot_state
+        slot = self.n % self.RING
+        self.n += 1
+        self.state_done[slot].synchronize()  # the copy that last read this buffer has run
+        self.state_host[slot].copy_(torch.tensor([pos, write_index, head, hlen, hstart, 0, 0, 0], dtype=torch.int32))
+        self.state_dev.copy_(self.state_host[slot], non_blocking=True)
+        self.state_done[slot].record()
+        B = int(token_id.numel())
+        key = (B,) + tuple((lc.arena.handle.value if hasattr(lc.arena.handle, "value") else id(lc.arena),
+                            lc._arena_k.data_ptr(), sg.table[0].data_ptr() if sg.table is not None else 0,
+                            sg.table[1:] if sg.table is not None else None) for lc, sg in zip(cache.layers, segs))
+        if self.tok.numel() != B:
+            self.tok = torch.zeros((B,), dtype=torch.long, device=model.device)
+        self.tok.copy_(token_id.reshape(-1).to(device=model.device, dtype=torch.long), non_blocking=True)
+        if key != self.key or self.graph is None:
+            self._capture(segs)
+            self.key = key
+            self.captures += 1
+        else:
+            self.graph.replay()
+            self.replays += 1
+        return self.logits.clone()
+
+    def _forward(self, segs) -> torch.Tensor:
+        model, cache = self.model, self.cache
+        x = F.embedding(self.tok.view(-1, 1), model.params["embed_tokens.weight"])
+        for i, layer in enumerate(model.layers):
+            lc, sg = cache.layer(i), segs[i]
+            x = layer(x, lc, 0, attn=lambda q, k, v, lc=lc, sg=sg: self._attention(lc, sg, q, k, v))
+        x = _layer_norm(x, model.params["norm.weight"], model.params["norm.bias"], model.config.norm_eps)
+        return model._lm_head(x)[:, 0, :]
+
+    def _attention(self, lc, segs, q, k, v) -> torch.Tensor:
+        B, H, L, D = (int(t) for t in q.shape)
+        qc, kc, vc = _as(q, lc.device, lc.dtype), _as(k, lc.device, lc.dtype), _as(v, lc.device, lc.dtype)
+        q_rot = torch.empty((B, H, L, D), dtype=torch.float32, device=lc.device)
+        native.check(
+            native.lib().rfsn_rope_append_step(
+                qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), native.dtype_code(lc.dtype), lc.inv_freq().data_ptr(),
+                self.state_dev.data_ptr(), B, H, lc.num_kv_heads, L, D, q_rot.data_ptr(), lc.arena.handle, 0,
+                lc.config.hot_capacity, native.stream_ptr()),
+            "rfsn_rope_append_step",
+        )
+        return paged_attention(lc, q_rot, 0, segs, workspace=self.workspace, step_state=self.state_dev)
+
+    def _capture(self, segs) -> None:
+        """Run this step once op by op on a side stream (the warm-up torch asks
+        for before a capture; it also produces this step's result), then capture."""
+        model = self.model
+        ws_bytes = native.workspace_bytes(int(self.tok.numel()), model.config.num_heads, model.config.num_kv_heads, 1,
+                                          model.config.head_dim, 0)
+        self.workspace.get(ws_bytes)
+        side = torch.cuda.Stream(device=model.device)
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            logits = self._forward(segs)
+        torch.cuda.current_stream().wait_stream(side)
+        self.graph = None
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            self.logits = self._forward(segs)
+        self.graph = graph
+        # the capture recorded work without running it: this step's result is the warm-up's
+        self.logits.copy_(logits)
 
 
 RFSNMLX = RFSNModel  # the reference's class name

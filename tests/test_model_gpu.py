@@ -96,6 +96,7 @@ def test_bf16_model_prefill_chunks_and_decode_run_on_tensor_core_paths(tmp_path,
                      model_dtype="bfloat16", runtime_mode=RuntimeMode.ARCHIVED, disk_cache_dir=str(tmp_path),
                      session_id="bf16")
     model = M.RFSNModel(cfg, device="cuda", seed=7)
+    model.use_graphs = False  # every attention call goes through attention_step (recorded here)
     cache = RFSNCache(cfg, batch_size=1, device="cuda")
     dense = _DenseModel(model)
     prompt = torch.randint(0, 256, (1, 600), generator=torch.Generator().manual_seed(8))
@@ -197,3 +198,72 @@ class _DenseModel:
         x = _layer_norm(x, p["norm.weight"], p["norm.bias"], cfg.norm_eps)
         self.pos += L
         return (x @ p["embed_tokens.weight"].T).float()
+
+
+def test_decode_graph_matches_op_by_op_decode(tmp_path):
+    """The captured whole-model decode step (device step state, re-captured after
+    every seal) against op-by-op decoding of the same model and tokens: equal
+    cache states; logits equal up to bf16 noise (the graph's decode kernel plans
+    its splits for the largest hot window, so float32 sums run in another order)."""
+    from rfsn_b200.cache import RFSNCache
+    from rfsn_b200.config import RFSNConfig, RuntimeMode
+    from rfsn_b200.model import RFSNModel
+
+    def make(use_graphs, sub):
+        cfg = RFSNConfig(hidden_dim=1024, num_heads=8, num_kv_heads=2, head_dim=128, num_layers=3, vocab_size=512,
+                         hot_capacity=128, block_size_seq=64, warm_capacity=4096, rope_base=10000.0,
+                         ffn_multiplier=2, model_dtype="bfloat16", runtime_mode=RuntimeMode.ARCHIVED,
+                         disk_cache_dir=str(tmp_path / sub), session_id=sub)
+        m = RFSNModel(cfg, device="cuda", seed=11)
+        m.use_graphs = use_graphs
+        return m, RFSNCache(cfg, batch_size=1, device="cuda")
+
+    eager, c_e = make(False, "eager")
+    graphed, c_g = make(True, "graph")
+    prompt = torch.randint(0, 512, (1, 100), generator=torch.Generator().manual_seed(12))
+    le, lg = eager.prefill(prompt, c_e), graphed.prefill(prompt, c_g)
+    tok = torch.argmax(le[:, -1], dim=-1).to(torch.int32)
+    for pos in range(100, 100 + 150):  # seals every 64 tokens once the 128-token ring is full
+        oe = eager.decode_step(tok, c_e, pos)
+        og = graphed.decode_step(tok, c_g, pos)
+        _close_bf16(og[0].float(), oe[0].float())
+        for a, b in zip(c_e.layers, c_g.layers):
+            assert (a.hot_head_index, a.hot_seq_len, a.hot_start) == (b.hot_head_index, b.hot_seq_len, b.hot_start)
+            assert [(m.logical_start, m.logical_end) for m in a.block_manager.iter_blocks(layer_id=a.layer_id)] == \
+                   [(m.logical_start, m.logical_end) for m in b.block_manager.iter_blocks(layer_id=b.layer_id)]
+        tok = torch.argmax(oe, dim=-1).to(torch.int32)  # both models are fed the same tokens
+    g = graphed._graph
+    assert g is not None and g.replays > 100 and 2 <= g.captures <= 8, (g.replays, g.captures)
+    graphed._graph.workspace.check()
+
+
+def test_decode_graph_falls_back_when_blocks_are_cold(tmp_path):
+    """A warm capacity below the archived context leaves cold blocks: the step
+    runs op by op (reloads included) and matches the op-by-op model exactly."""
+    from rfsn_b200.cache import RFSNCache
+    from rfsn_b200.config import RFSNConfig, RuntimeMode
+    from rfsn_b200.model import RFSNModel
+
+    def make(use_graphs, sub):
+        cfg = RFSNConfig(hidden_dim=512, num_heads=4, num_kv_heads=1, head_dim=128, num_layers=1, vocab_size=256,
+                         hot_capacity=64, block_size_seq=32, warm_capacity=64, cold_capacity=4096, rope_base=10000.0,
+                         ffn_multiplier=2, model_dtype="bfloat16", runtime_mode=RuntimeMode.ARCHIVED,
+                         disk_cache_dir=str(tmp_path / sub), session_id=sub)
+        m = RFSNModel(cfg, device="cuda", seed=13)
+        m.use_graphs = use_graphs
+        return m, RFSNCache(cfg, batch_size=1, device="cuda")
+
+    eager, c_e = make(False, "e")
+    graphed, c_g = make(True, "g")
+    prompt = torch.randint(0, 256, (1, 200), generator=torch.Generator().manual_seed(14))
+    le = eager.prefill(prompt, c_e)
+    graphed.prefill(prompt, c_g)
+    tok = torch.argmax(le[:, -1], dim=-1).to(torch.int32)
+    for pos in range(200, 210):
+        c_e.layer(0).residency_manager.wait_for_prefetches(c_e.layer(0), timeout=30.0)
+        c_g.layer(0).residency_manager.wait_for_prefetches(c_g.layer(0), timeout=30.0)
+        oe = eager.decode_step(tok, c_e, pos)
+        og = graphed.decode_step(tok, c_g, pos)
+        assert torch.equal(oe, og)
+        tok = torch.argmax(oe, dim=-1).to(torch.int32)
+    assert c_g.layer(0).residency_manager.get_metrics() == c_e.layer(0).residency_manager.get_metrics()
