@@ -269,7 +269,7 @@ def e2e_throughput(cache, w, world, owns_hot, steps, calls_per_step, peers=None)
     import torch
 
     from rfsn_b200 import _native as native
-    from rfsn_b200.layer import attention_step
+    from rfsn_b200.layer import GraphedDecodeStep
     from rfsn_b200.sharded import sharded_decode_step
 
     dt = cache.dtype
@@ -288,15 +288,24 @@ def e2e_throughput(cache, w, world, owns_hot, steps, calls_per_step, peers=None)
         dist.all_reduce(t)
         pos = int(t.item())
 
+    graphed = None
+    if world == 1:
+        # one graph replay per call: H2D of the token's q/k/v, RoPE + append,
+        # paged attention, D2H of the output (rfsn_b200.layer.GraphedDecodeStep)
+        graphed = GraphedDecodeStep(cache, H)
+        graphed.q_host.copy_(q_h)
+        graphed.k_host.copy_(k_h)
+        graphed.v_host.copy_(v_h)
+
     def call(p):
+        if graphed is not None:
+            graphed.step(p)
+            return
         q = q_h.to(cache.device, non_blocking=True)
         k = k_h.to(cache.device, non_blocking=True)
         v = v_h.to(cache.device, non_blocking=True)
-        if world == 1:
-            out = attention_step(q, k, v, cache, p)
-        else:
-            out = sharded_decode_step(cache, q, k if owns_hot else None, v if owns_hot else None, p, owns_hot=owns_hot,
-                                      peers=peers)
+        out = sharded_decode_step(cache, q, k if owns_hot else None, v if owns_hot else None, p, owns_hot=owns_hot,
+                                  peers=peers)
         out_h.copy_(out, non_blocking=True)
         torch.cuda.current_stream().synchronize()
 
@@ -305,12 +314,15 @@ def e2e_throughput(cache, w, world, owns_hot, steps, calls_per_step, peers=None)
     pos += 3
     barrier(world)
     before = native.launch_count()
+    replays0 = graphed.replays if graphed is not None else 0
     t0 = time.perf_counter()
     n = steps * calls_per_step
     for i in range(n):
         call(pos + i)
     elapsed = time.perf_counter() - t0
     launches = native.launch_count() - before
+    if graphed is not None:  # kernels replayed inside the graph are not host launches
+        launches += graphed.graph_kernels * (graphed.replays - replays0)
     barrier(world)
     h2d = q_h.numel() * q_h.element_size() + (k_h.numel() * k_h.element_size() * 2 if owns_hot else 0)
     d2h = out_h.numel() * out_h.element_size()
@@ -488,7 +500,8 @@ def run_ours(args, w):
                 "h2d_bytes_per_step": h2d * e2e_calls,
                 "d2h_bytes_per_step": d2h * e2e_calls,
                 "calls_per_step": e2e_calls,
-                "api": "rfsn_b200.layer.attention_step" if world == 1 else "rfsn_b200.sharded.sharded_decode_step",
+                "api": "rfsn_b200.layer.GraphedDecodeStep (host buffers in/out, one graph replay per call)"
+                if world == 1 else "rfsn_b200.sharded.sharded_decode_step",
             },
             "gpu_launches": launches,
             "e2e_gpu_launches": e_launches,

@@ -21,7 +21,7 @@ from .attention_exact import (  # noqa: F401
     run_exact_attention,
     run_segmented_attention,
 )
-from .layer import attention_step, build_rope_tables  # noqa: F401
+from .layer import GraphedDecodeStep, attention_step, build_rope_tables  # noqa: F401
 from .model import RFSNMLX, RFSNModel  # noqa: F401
 
 __all__ = [
@@ -40,6 +40,7 @@ __all__ = [
     "BlockStorage",
     "build_rope_tables",
     "attention_step",
+    "GraphedDecodeStep",
     "run_segmented_attention",
     "run_exact_attention",
     "exact_attention",

@@ -12,7 +12,7 @@ query head h to KV head h // groups).
 
 from __future__ import annotations
 
-from typing import Tuple
+from typing import Optional, Tuple
 
 import numpy as np
 import torch
@@ -47,3 +47,144 @@ def attention_step(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cache: Lay
         cache.maybe_prefetch_for_decode(start_pos)
     segments = cache.get_attention_segments()
     return paged_attention(cache, q_rot, start_pos, segments)
+
+
+def capture_graph(fn, stream: torch.cuda.Stream) -> torch.cuda.CUDAGraph:
+    """Capture ``fn()`` into a new CUDA graph on ``stream``. Unlike the
+    ``torch.cuda.graph`` context manager this runs no garbage collection or
+    cache release first, which would cost tens to hundreds of milliseconds at
+    every re-capture of a decode step."""
+    graph = torch.cuda.CUDAGraph()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        graph.capture_begin()
+        try:
+            fn()
+        finally:
+            graph.capture_end()
+    torch.cuda.current_stream().wait_stream(stream)
+    return graph
+
+
+class GraphedDecodeStep:
+    """One decode token of one layer, host buffers in and out, as one CUDA graph.
+
+    Fill ``q_host`` [B, H, 1, D], ``k_host`` / ``v_host`` [B, Hkv, 1, D]
+    (pinned, cache dtype) and call ``step(pos)``: the host runs the cache
+    bookkeeping of ``attention_step`` (seal rule, append counters, prefetch
+    hook, segment walk), writes the step state, and replays a graph holding
+    one host-to-device copy (step state, q, k and v share one pinned staging
+    buffer), the fused RoPE/append and the paged decode kernel reading that
+    state, and the copy of the float32 output back to ``out_host``, which is
+    returned after the step completes. The graph is captured again when the
+    page table or the arena changes; when archived blocks are cold or a
+    prefetch is in flight the step runs ``attention_step`` op by op instead.
+    Needs bf16/f16 K/V, head_dim 128 and <= 4 query heads per KV head (the
+    tensor-core decode kernel)."""
+
+    def __init__(self, cache: LayerKVCache, q_heads: int) -> None:
+        from . import _native as native
+
+        self.cache = cache
+        B, Hkv, D = cache.batch_size, cache.num_kv_heads, cache.config.head_dim
+        self.shape_q = (B, q_heads, 1, D)
+        shape_kv = (B, Hkv, 1, D)
+        self.supported = (cache.dtype in (torch.bfloat16, torch.float16) and D == 128 and q_heads % Hkv == 0
+                          and q_heads // Hkv <= 4)
+        dev = cache.device
+        es = torch.empty((), dtype=cache.dtype).element_size()
+        align = lambda n: (n + 255) // 256 * 256  # noqa: E731
+        n_state = align(4 * native.STEP_STATE_LEN)
+        n_q = align(B * q_heads * D * es)
+        n_kv = align(B * Hkv * D * es)
+        total = n_state + n_q + 2 * n_kv
+        self.stage_host = torch.zeros(total, dtype=torch.uint8).pin_memory()
+        self.stage_dev = torch.zeros(total, dtype=torch.uint8, device=dev)
+
+        def views(buf):
+            st = buf[:4 * native.STEP_STATE_LEN].view(torch.int32)
+            o = n_state
+            q = buf[o:o + B * q_heads * D * es].view(cache.dtype).view(self.shape_q)
+            o += n_q
+            k = buf[o:o + B * Hkv * D * es].view(cache.dtype).view(shape_kv)
+            o += n_kv
+            v = buf[o:o + B * Hkv * D * es].view(cache.dtype).view(shape_kv)
+            return st, q, k, v
+
+        self.state_host, self.q_host, self.k_host, self.v_host = views(self.stage_host)
+        self.state_dev, self.q_dev, self.k_dev, self.v_dev = views(self.stage_dev)
+        self.out_host = torch.zeros(self.shape_q, dtype=torch.float32).pin_memory()
+        self.workspace = native.Workspace(dev)
+        self.workspace.get(native.workspace_bytes(B, q_heads, Hkv, 1, D, 0))
+        self.stream = torch.cuda.Stream(device=dev)
+        self.graph: Optional[torch.cuda.CUDAGraph] = None
+        self.key = None
+        self.replays = self.captures = self.fallbacks = 0
+        self.graph_kernels = 0
+
+    def _eligible(self) -> bool:
+        c = self.cache
+        return self.supported and not c.residency_manager.has_pending and c.all_blocks_resident()
+
+    def _body(self, segs) -> torch.Tensor:
+        from . import _native as native
+        from .cache import paged_attention
+
+        c = self.cache
+        self.stage_dev.copy_(self.stage_host, non_blocking=True)
+        B, H, L, D = self.shape_q
+        q_rot = torch.empty(self.shape_q, dtype=torch.float32, device=c.device)
+        native.check(
+            native.lib().rfsn_rope_append_step(
+                self.q_dev.data_ptr(), self.k_dev.data_ptr(), self.v_dev.data_ptr(), native.dtype_code(c.dtype),
+                c.inv_freq().data_ptr(), self.state_dev.data_ptr(), B, H, c.num_kv_heads, 1, D, q_rot.data_ptr(),
+                c.arena.handle, 0, c.config.hot_capacity, native.stream_ptr()),
+            "rfsn_rope_append_step",
+        )
+        out = paged_attention(c, q_rot, 0, segs, workspace=self.workspace, step_state=self.state_dev)
+        self.out_host.copy_(out, non_blocking=True)
+        return out
+
+    def step(self, pos: int) -> torch.Tensor:
+        from . import _native as native
+
+        c = self.cache
+        if not self._eligible():
+            self.fallbacks += 1
+            out = attention_step(self.q_host.to(c.device, non_blocking=True),
+                                 self.k_host.to(c.device, non_blocking=True),
+                                 self.v_host.to(c.device, non_blocking=True), c, pos)
+            self.out_host.copy_(out, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+            return self.out_host
+        # attention_step's host part for one token (layer.py:134-139)
+        c.evict_for_append(1)
+        write_index = c.hot_write_index
+        c._check_append(1)
+        c.hot_seq_len += 1
+        c.maybe_prefetch_for_decode(pos)
+        segs = c.get_attention_segments()
+        head, hlen, hstart = segs.hot_state
+        st = self.state_host
+        st[0], st[1], st[2], st[3], st[4] = pos, write_index, head, hlen, hstart
+        key = (c.arena.handle.value, c._arena_k.data_ptr(),
+               (segs.table[0].data_ptr(),) + tuple(segs.table[1:]) if segs.table is not None else None)
+        if key != self.key or self.graph is None:
+            # run this step op by op on the side stream first (the warm-up a
+            # capture wants; it also produces this step's result), then capture
+            self.stream.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(self.stream):
+                self._body(segs)
+            torch.cuda.current_stream().wait_stream(self.stream)
+            self.graph = None
+            before = native.launch_count()
+            graph = capture_graph(lambda: self._body(segs), self.stream)
+            self.graph_kernels = native.launch_count() - before  # this library's kernels per replay
+            self.graph, self.key = graph, key
+            self.captures += 1
+            torch.cuda.current_stream().synchronize()
+            return self.out_host
+        self.graph.replay()
+        self.replays += 1
+        torch.cuda.current_stream().synchronize()
+        return self.out_host

@@ -31,7 +31,7 @@ import torch.nn.functional as F
 from . import _native as native
 from .cache import RFSNCache, _as, paged_attention
 from .config import RFSNConfig, RuntimeMode, resolve_dtype
-from .layer import attention_step
+from .layer import attention_step, capture_graph
 
 ArrayLike = Union[np.ndarray, torch.Tensor]
 
@@ -324,6 +324,7 @@ class _DecodeGraph:
         self.state_done = [torch.cuda.Event() for _ in range(self.RING)]
         self.n = 0
         self.workspace = native.Workspace(dev)
+        self.stream = torch.cuda.Stream(device=dev)
         self.graph: Optional[torch.cuda.CUDAGraph] = None
         self.key = None
         self.logits: Optional[torch.Tensor] = None
@@ -405,16 +406,16 @@ class _DecodeGraph:
         ws_bytes = native.workspace_bytes(int(self.tok.numel()), model.config.num_heads, model.config.num_kv_heads, 1,
                                           model.config.head_dim, 0)
         self.workspace.get(ws_bytes)
-        side = torch.cuda.Stream(device=model.device)
+        side = self.stream
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(side):
             logits = self._forward(segs)
         torch.cuda.current_stream().wait_stream(side)
+        logits.record_stream(torch.cuda.current_stream())  # read below on this stream
         self.graph = None
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            self.logits = self._forward(segs)
-        self.graph = graph
+        out = {}
+        self.graph = capture_graph(lambda: out.setdefault("logits", self._forward(segs)), side)
+        self.logits = out["logits"]
         # the capture recorded work without running it: this step's result is the warm-up's
         self.logits.copy_(logits)
 

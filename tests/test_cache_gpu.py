@@ -156,3 +156,39 @@ def test_demote_to_disk_and_restore_session():
             other = _cfg("bfloat16", H, Hkv, D, 64, 64, tmp, warm=1 << 12)
             other.session_id = "nobody"
             RFSNCache(other, 1, restore=True).restore_from_disk()
+
+
+def test_graphed_decode_step_matches_attention_step():
+    """rfsn_b200.layer.GraphedDecodeStep (host buffers, one graph replay per call,
+    re-captured after each seal) against attention_step on a twin cache."""
+    from rfsn_b200 import LayerKVCache
+    from rfsn_b200.layer import GraphedDecodeStep, attention_step
+
+    with tempfile.TemporaryDirectory() as tmp:
+        cfg = _cfg("bfloat16", 16, 4, 128, 256, 96, tmp)
+        caches = [LayerKVCache(cfg, 1, 16, 4, layer_id=0, session_id=f"g{i}") for i in range(2)]
+        gen = torch.Generator(device="cuda").manual_seed(21)
+        for n in (256, 200):  # prefill-like appends: seal rule + archived blocks
+            k = torch.randn((1, 4, n, 128), generator=gen, device="cuda").to(torch.bfloat16)
+            v = torch.randn((1, 4, n, 128), generator=gen, device="cuda").to(torch.bfloat16)
+            for c in caches:
+                c.evict_for_append(n)
+                c.append_exact(k, v)
+        eager, graphed_cache = caches
+        step = GraphedDecodeStep(graphed_cache, 16)
+        pos = eager.hot_end
+        for i in range(300):  # crosses several 96-token seals
+            q = torch.randn((1, 16, 1, 128), generator=gen, device="cuda").to(torch.bfloat16)
+            k = torch.randn((1, 4, 1, 128), generator=gen, device="cuda").to(torch.bfloat16)
+            v = torch.randn((1, 4, 1, 128), generator=gen, device="cuda").to(torch.bfloat16)
+            want = attention_step(q, k, v, eager, pos).cpu()
+            step.q_host.copy_(q.cpu())
+            step.k_host.copy_(k.cpu())
+            step.v_host.copy_(v.cpu())
+            got = step.step(pos)
+            assert float((got - want).abs().max()) <= 1e-5, i
+            assert (eager.hot_head_index, eager.hot_seq_len, eager.hot_start) == \
+                   (graphed_cache.hot_head_index, graphed_cache.hot_seq_len, graphed_cache.hot_start)
+            pos += 1
+        assert step.replays > 250 and step.captures >= 3 and step.fallbacks == 0, (step.replays, step.captures)
+        step.workspace.check()
