@@ -211,6 +211,8 @@ __device__ __forceinline__ void peer_store_and_merge(const PeerParams& peer, con
     if (lse != nullptr && d4 == 0) lse[om.row(group, sl)] = W > 0.f ? M + logf(W) : -CUDART_INF_F;
 }
 
+constexpr int kMergeDepth = 24;  // independent loads in flight per thread in the split merge
+
 __device__ __forceinline__ void finish_splits(const WsView& ws, int counter_idx, int part_base, int split_stride,
                                               int splits, int slot0, int nslots, int head_dim, const OutMap& om,
                                               int bh, float* out, float* lse, int* flag, float* sbuf, int bar_id,
@@ -226,6 +228,22 @@ __device__ __forceinline__ void finish_splits(const WsView& ws, int counter_idx,
         named_barrier_sync(bar_id, nthreads);
         if (!*flag) return;
         __threadfence();
+    }
+    // The merge is a chain of L2 round trips (arrival atomic, m/l, O). Each
+    // thread's first kMergeDepth partial-output vectors are requested now, so
+    // they travel while the weights are computed; the rest follow in chunks of
+    // kMergeDepth independent loads.
+    const int d4n = head_dim >> 2;
+    const bool vec4 = (head_dim & 3) == 0;
+    const int items = vec4 ? nslots * d4n : 0;
+    const size_t o_stride = (size_t)split_stride * d4n;
+    float4 ov[kMergeDepth];
+    if (tid < items) {
+        const int sl = tid / d4n, d4 = tid - sl * d4n;
+        const float4* base = reinterpret_cast<const float4*>(ws.o) + (size_t)(part_base + slot0 + sl) * d4n + d4;
+#pragma unroll
+        for (int u = 0; u < kMergeDepth; ++u) ov[u] = u < splits ? __ldcg(base + (size_t)u * o_stride)
+                                                                 : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     float* wts = sbuf;                          // [nslots][splits] m_s, then weights
     float* ls = sbuf + nslots * splits;         // [nslots][splits] l_s
@@ -260,36 +278,29 @@ __device__ __forceinline__ void finish_splits(const WsView& ws, int counter_idx,
         }
     }
     named_barrier_sync(bar_id, nthreads);
-    if ((head_dim & 3) == 0) {
-        const int d4n = head_dim >> 2;
-        for (int idx = tid; idx < nslots * d4n; idx += nthreads) {
+    if (vec4) {
+        for (int idx = tid; idx < items; idx += nthreads) {
             const int sl = idx / d4n, d4 = idx - sl * d4n;
             const float* w = wts + sl * splits;
             const float4* base = reinterpret_cast<const float4*>(ws.o) +
                                  (size_t)(part_base + slot0 + sl) * d4n + d4;
-            const size_t stride = (size_t)split_stride * d4n;
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            int s = 0;
-            for (; s + 8 <= splits; s += 8) {
-                float4 v[8];
+            for (int s0 = 0; s0 < splits; s0 += kMergeDepth) {
+                if (idx != tid || s0 != 0) {  // the first chunk of the first item is already in flight
 #pragma unroll
-                for (int u = 0; u < 8; ++u) v[u] = __ldcg(base + (size_t)(s + u) * stride);
-#pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    const float c = w[s + u];
-                    acc.x += c * v[u].x;
-                    acc.y += c * v[u].y;
-                    acc.z += c * v[u].z;
-                    acc.w += c * v[u].w;
+                    for (int u = 0; u < kMergeDepth; ++u) {
+                        ov[u] = s0 + u < splits ? __ldcg(base + (size_t)(s0 + u) * o_stride)
+                                                : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
                 }
-            }
-            for (; s < splits; ++s) {
-                const float4 v = __ldcg(base + (size_t)s * stride);
-                const float c = w[s];
-                acc.x += c * v.x;
-                acc.y += c * v.y;
-                acc.z += c * v.z;
-                acc.w += c * v.w;
+#pragma unroll
+                for (int u = 0; u < kMergeDepth; ++u) {
+                    const float c = s0 + u < splits ? w[s0 + u] : 0.f;
+                    acc.x += c * ov[u].x;
+                    acc.y += c * ov[u].y;
+                    acc.z += c * ov[u].z;
+                    acc.w += c * ov[u].w;
+                }
             }
             const float inv = 1.f / fmaxf(totals[sl], 1e-9f);
             float4 r = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
