@@ -616,7 +616,19 @@ rfsn_status rfsn_workspace_check(void* workspace, void* stream, int64_t timeout_
     if (word != 0) {
         const int zero = 0;
         RFSN_CUDA(cudaMemcpy(workspace, &zero, sizeof(int), cudaMemcpyHostToDevice));
-        set_error("attention kernel reported device error %d (bounded wait expired)", word);
+        if (word == kDevErrPeerTimeout) {
+            set_error("attention kernel: the cross-GPU merge timed out waiting for a peer's partial results");
+            return RFSN_ERR_TIMEOUT;
+        }
+        if (word == kDevErrTimeout) {
+            set_error("attention kernel: a bounded pipeline wait expired");
+            return RFSN_ERR_TIMEOUT;
+        }
+        if (word == kDevErrBadTable) {
+            set_error("attention kernel: a page-table record or step state points outside the arena");
+            return RFSN_ERR_DEVICE;
+        }
+        set_error("attention kernel reported device error %d", word);
         return RFSN_ERR_DEVICE;
     }
     return RFSN_OK;

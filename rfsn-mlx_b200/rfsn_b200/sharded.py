@@ -128,9 +128,10 @@ class PeerGroup:
             if dist.get_backend(group) == "nccl":
                 out = torch.empty(self.world * nbytes, dtype=torch.uint8, device=t.device)
                 dist.all_gather_into_tensor(out, t, group=group)
-            else:
-                parts = [torch.empty_like(t) for _ in range(self.world)]
-                dist.all_gather(parts, t, group=group)
+            else:  # gloo exchanges host tensors
+                tc = t.cpu()
+                parts = [torch.empty_like(tc) for _ in range(self.world)]
+                dist.all_gather(parts, tc, group=group)
                 out = torch.cat(parts)
             raw = bytes(out.cpu().numpy().tobytes())
         table = (ctypes.c_ubyte * len(raw)).from_buffer_copy(raw)

@@ -206,3 +206,66 @@ def test_sharded_decode_step_two_gpus(mode):
     for rank in range(world):
         for out in got[rank]:
             assert float(np.abs(out - ref).max()) <= 2e-3
+
+
+def _silent_peer_worker(rank, port, results):
+    """Two processes on cuda:0 form a world-2 peer group (gloo for the handle
+    exchange). Rank 1 never runs the attention kernel; rank 0's fused merge must
+    give up after its short timeout, report it through the workspace error word,
+    and leave the context usable."""
+    try:
+        import sys
+
+        root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+        sys.path[:0] = [root, os.path.join(root, "rfsn-mlx_b200"), os.path.join(root, "tests")]
+        import torch
+        import torch.distributed as dist
+
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(0)
+        dist.init_process_group("gloo", rank=rank, world_size=2, timeout=datetime.timedelta(seconds=60))
+        from rfsn_b200 import _native as native
+        from rfsn_b200.cache import paged_attention
+        from rfsn_b200.sharded import PeerGroup
+
+        q, k, v, total = _data()
+        with tempfile.TemporaryDirectory() as tmp:
+            cache = _shard_cache(rank, 2, k, v, torch.device("cuda", 0), tmp)
+            peers = PeerGroup(HKV, D, timeout_s=0.05)
+            msg = "no call"
+            if rank == 0:
+                qd = torch.from_numpy(q).cuda()
+                segs = cache.get_attention_segments()
+                paged_attention(cache, qd, total - 1, segs, peers=peers)
+                ws = native.default_workspace(torch.device("cuda", 0))
+                try:
+                    ws.check(timeout_s=30.0)
+                    msg = "no error reported"
+                except TimeoutError as exc:
+                    msg = "timeout: " + str(exc)
+                # the context still works: a plain local call and a clean error word
+                out = paged_attention(cache, qd, total - 1, segs)
+                torch.cuda.synchronize()
+                ws.check()
+                msg += f" | finite={bool(torch.isfinite(out).all())}"
+            dist.barrier()  # rank 1 stays idle until rank 0 is done
+            peers.close()
+            results.put((rank, msg))
+        dist.destroy_process_group()
+    except Exception:
+        results.put((rank, "crash: " + traceback.format_exc()))
+
+
+def test_peer_merge_timeout_is_reported_and_context_survives():
+    ctx = mp.get_context("spawn")
+    results = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_silent_peer_worker, args=(r, port, results)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(results.get(timeout=300) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+    assert got[0].startswith("timeout:") and "the cross-GPU merge timed out" in got[0], got[0]
+    assert got[0].endswith("finite=True"), got[0]
+    assert got[1] == "no call", got[1]
