@@ -424,13 +424,41 @@ rfsn_status rfsn::paged_attention_impl(const rfsn_arena* arena, const float* q, 
         return RFSN_ERR_UNSUPPORTED;
     }
     if (use_prefill) {
-        const WsLayout w = ws_layout(a.groups, 1, 1, a.slots_ws, 128);
+        // One CTA per (query block, KV head) streams the whole causal key range. When
+        // there are too few of them to keep the SMs busy (one CTA per SM; a short chunk
+        // over a long context), each query block's key stream is split into S even
+        // ranges and the last CTA of the block merges the results. With many units the
+        // causal spread of their lengths already fills the last wave and splitting
+        // only adds overhead (measured on the 2048-token chunks of a 32K prompt).
+        const int nqb = (q_len + 128 / a.G - 1) / (128 / a.G);
+        const int units = nqb * a.groups;
+        const int avg_tiles = (q_pos0 + q_len / 2) / 128;
+        auto wave_eff = [&](int n) { return (double)n / ((double)((n + sms - 1) / sms) * sms); };
+        int splits = 1;
+        double best = wave_eff(units);
+        if (best < 0.75) {
+            for (int cand = 2; cand <= 4; ++cand) {
+                if (avg_tiles / cand < 16 || units > kMaxCounters) break;
+                const double e = wave_eff(units * cand);
+                if (e > best + 0.05) {
+                    best = e;
+                    splits = cand;
+                }
+            }
+        }
+        WsLayout w = ws_layout(a.groups, 1, splits > 1 ? nqb * splits : 1, splits > 1 ? 128 : a.slots_ws, 128);
+        if (w.total > workspace_bytes && splits > 1) {
+            splits = 1;
+            w = ws_layout(a.groups, 1, 1, a.slots_ws, 128);
+        }
         if (w.total > workspace_bytes) {
             set_error("attention workspace too small: need %zu bytes, have %zu", w.total, workspace_bytes);
             return RFSN_ERR_OVERFLOW;
         }
         PrefillParams pp;
         memset(&pp, 0, sizeof(pp));
+        pp.splits = splits;
+        pp.nqb = nqb;
         pp.q = q;
         pp.out = out;
         pp.lse = lse;

@@ -48,7 +48,8 @@ struct PrefillParams {
     int rows;                 // arena rows per head
     int batch, q_heads, kv_heads, q_len, q_pos0, groups_per_kv;
     float qscale;             // 1/sqrt(D) * log2(e)
-    WsView ws;                // error word only
+    int splits, nqb;          // key-range splits per query block (grid z), query blocks (grid x)
+    WsView ws;                // error word; with splits > 1 also counters and partial (O, LSE)
 };
 
 namespace generic {

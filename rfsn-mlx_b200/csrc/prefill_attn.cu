@@ -85,6 +85,7 @@ struct Smem {
     int2 tinfo[NINFO];    // {kpos0, nvalid} per tile (ring); nvalid < 0 marks the end of the key stream
     uint32_t tmem;
     int abort;
+    int flag;  // this CTA merges the key-range splits of its query block
 };
 
 // (a, b) -> packed 16-bit high parts and packed 16-bit residuals (a = hi + lo to
@@ -164,6 +165,14 @@ struct TileWalk {
     }
 };
 
+// Tiles in the CTA's key stream (the walk above, counted).
+__device__ __forceinline__ int count_tiles(const PrefillParams& p, int qlast) {
+    TileWalk w;
+    int kpos0, row, nvalid, n = 0;
+    while (w.next(p, qlast, kpos0, row, nvalid)) ++n;
+    return n;
+}
+
 // One K or V tile -> a stage (two 64-column halves): 64-row boxes for a full
 // tile, 8-row boxes for a ragged span end.
 __device__ __forceinline__ void load_tile(uint8_t (*dst)[TILE_HALF], const CUtensorMap* m64, const CUtensorMap* m8,
@@ -201,6 +210,9 @@ prefill_attn_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
     const int b = bh / p.kv_heads, hk = bh % p.kv_heads;
     const int pos_base = qb * ppc;                            // first chunk position of the CTA
     const int qlast = p.q_pos0 + min(pos_base + ppc, p.q_len) - 1;  // causal limit of the CTA
+    // Key-range split: CTA z of a query block streams tiles [t0, t1) of its key
+    // stream (even shares); the last CTA to finish merges the partial results.
+    const int split = blockIdx.z;
 
     // ---- set-up: zero the K/V stages (rows past a ragged span end stay finite),
     //      barriers, TMEM ----
@@ -247,9 +259,17 @@ prefill_attn_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
         if (lane == 0) {
             prefetch_tmap(&mapK64);
             prefetch_tmap(&mapK8);
+            int t0 = 0, t1 = 1 << 30;
+            if (p.splits > 1) {
+                const int ntile = count_tiles(p, qlast);
+                t0 = (int)((long long)split * ntile / p.splits);
+                t1 = (int)((long long)(split + 1) * ntile / p.splits);
+            }
             TileWalk walk;
-            int it = 0, kpos0, row, nvalid;
+            int it = 0, gi = -1, kpos0, row, nvalid;
             while (walk.next(p, qlast, kpos0, row, nvalid)) {
+                if (++gi < t0) continue;
+                if (gi >= t1) break;
                 const int s = it % KST;
                 // stage free once S(it - KST) is done
                 if (it >= KST && !mbar_wait_bounded(&sm.k_empty[s], ((it / KST) + 1) & 1, &sm.abort)) {
@@ -284,9 +304,17 @@ prefill_attn_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
         if (lane == 0) {
             prefetch_tmap(&mapV64);
             prefetch_tmap(&mapV8);
+            int t0 = 0, t1 = 1 << 30;
+            if (p.splits > 1) {
+                const int ntile = count_tiles(p, qlast);
+                t0 = (int)((long long)split * ntile / p.splits);
+                t1 = (int)((long long)(split + 1) * ntile / p.splits);
+            }
             TileWalk walk;
-            int it = 0, kpos0, row, nvalid;
+            int it = 0, gi = -1, kpos0, row, nvalid;
             while (walk.next(p, qlast, kpos0, row, nvalid)) {
+                if (++gi < t0) continue;
+                if (gi >= t1) break;
                 const int s = it % VST;
                 // stage free once PV(it - VST) is done
                 if (it >= VST && !mbar_wait_bounded(&sm.v_empty[s], ((it / VST) + 1) & 1, &sm.abort)) {
@@ -509,25 +537,87 @@ prefill_attn_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
         const float lt = ok ? l + sm.red[0][ch ^ 1][r] : 0.f;
         float* dst = p.out + (((size_t)b * p.q_heads + h) * p.q_len + (row_ok ? qrow : 0)) * D + 64 * ch;
         const float inv = (ok && lt > 0.f) ? 1.f / lt : 0.f;
+        if (p.splits > 1) {
+            // this split's normalised output and natural-log LSE -> workspace; the last
+            // split CTA of the query block combines them (an empty range: LSE -inf)
+            const size_t unit = (size_t)bh * p.nqb + qb;
+            const size_t prow = (unit * p.splits + split) * BM + r;
+            float* po = p.ws.o + prow * D + 64 * ch;
 #pragma unroll 1
-        for (int cc = 0; cc < 2; ++cc) {
-            uint32_t rr[32];
-            tc::ld_32x32b_x32_sync(tO + 32 * cc, rr);
-            if (row_ok) {
+            for (int cc = 0; cc < 2; ++cc) {
+                uint32_t rr[32];
+                tc::ld_32x32b_x32_sync(tO + 32 * cc, rr);
 #pragma unroll
                 for (int jj = 0; jj < 32; jj += 4) {
-                    *reinterpret_cast<float4*>(dst + 32 * cc + jj) =
-                        ok ? make_float4(__uint_as_float(rr[jj]) * inv, __uint_as_float(rr[jj + 1]) * inv,
-                                         __uint_as_float(rr[jj + 2]) * inv, __uint_as_float(rr[jj + 3]) * inv)
-                           : make_float4(0.f, 0.f, 0.f, 0.f);
+                    *reinterpret_cast<float4*>(po + 32 * cc + jj) =
+                        make_float4(__uint_as_float(rr[jj]) * inv, __uint_as_float(rr[jj + 1]) * inv,
+                                    __uint_as_float(rr[jj + 2]) * inv, __uint_as_float(rr[jj + 3]) * inv);
                 }
             }
+            if (ch == 0) p.ws.m[prow] = (ok && lt > 0.f) ? (m + log2f(lt)) * 0.69314718055994531f : -CUDART_INF_F;
+            if (!ok && tid == 0 && it > 0) atomicExch(p.ws.error, kDevErrTimeout);
+            __threadfence();
+            named_barrier_sync(3, SOFTMAX_THREADS);
+            if (tid == 0) sm.flag = atomicAdd(&p.ws.counters[unit], 1) == p.splits - 1;
+            named_barrier_sync(3, SOFTMAX_THREADS);
+            if (sm.flag) {
+                __threadfence();
+                const size_t base = unit * p.splits * BM + r;
+                float M = -CUDART_INF_F;
+                for (int s = 0; s < p.splits; ++s) M = fmaxf(M, __ldcg(p.ws.m + base + (size_t)s * BM));
+                float acc[64];
+#pragma unroll
+                for (int d = 0; d < 64; ++d) acc[d] = 0.f;
+                float L = 0.f;
+                for (int s = 0; s < p.splits; ++s) {
+                    const float ls = __ldcg(p.ws.m + base + (size_t)s * BM);
+                    const float wgt = (M == -CUDART_INF_F) ? 0.f : exp2f((ls - M) * 1.4426950408889634f);
+                    L += wgt;
+                    const float4* src = reinterpret_cast<const float4*>(p.ws.o + (base + (size_t)s * BM) * D + 64 * ch);
+#pragma unroll
+                    for (int d4 = 0; d4 < 16; ++d4) {
+                        const float4 o4 = __ldcg(src + d4);
+                        acc[4 * d4] += wgt * o4.x;
+                        acc[4 * d4 + 1] += wgt * o4.y;
+                        acc[4 * d4 + 2] += wgt * o4.z;
+                        acc[4 * d4 + 3] += wgt * o4.w;
+                    }
+                }
+                const float invL = L > 0.f ? 1.f / L : 0.f;
+                if (row_ok) {
+#pragma unroll
+                    for (int d4 = 0; d4 < 16; ++d4) {
+                        *reinterpret_cast<float4*>(dst + 4 * d4) = make_float4(
+                            acc[4 * d4] * invL, acc[4 * d4 + 1] * invL, acc[4 * d4 + 2] * invL, acc[4 * d4 + 3] * invL);
+                    }
+                    if (ch == 0 && p.lse != nullptr) {
+                        p.lse[((size_t)b * p.q_heads + h) * p.q_len + qrow] =
+                            L > 0.f ? M + logf(L) : -CUDART_INF_F;
+                    }
+                }
+                if (tid == 0) p.ws.counters[unit] = 0;  // ready for the next call
+            }
+        } else {
+#pragma unroll 1
+            for (int cc = 0; cc < 2; ++cc) {
+                uint32_t rr[32];
+                tc::ld_32x32b_x32_sync(tO + 32 * cc, rr);
+                if (row_ok) {
+#pragma unroll
+                    for (int jj = 0; jj < 32; jj += 4) {
+                        *reinterpret_cast<float4*>(dst + 32 * cc + jj) =
+                            ok ? make_float4(__uint_as_float(rr[jj]) * inv, __uint_as_float(rr[jj + 1]) * inv,
+                                             __uint_as_float(rr[jj + 2]) * inv, __uint_as_float(rr[jj + 3]) * inv)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+                }
+            }
+            if (row_ok && ch == 0 && p.lse != nullptr) {
+                p.lse[((size_t)b * p.q_heads + h) * p.q_len + qrow] =
+                    (ok && lt > 0.f) ? (m + log2f(lt)) * 0.69314718055994531f : -CUDART_INF_F;
+            }
+            if (!ok && tid == 0 && it > 0) atomicExch(p.ws.error, kDevErrTimeout);
         }
-        if (row_ok && ch == 0 && p.lse != nullptr) {
-            p.lse[((size_t)b * p.q_heads + h) * p.q_len + qrow] =
-                (ok && lt > 0.f) ? (m + log2f(lt)) * 0.69314718055994531f : -CUDART_INF_F;
-        }
-        if (!ok && tid == 0 && it > 0) atomicExch(p.ws.error, kDevErrTimeout);
     }
     tc::fence_before_sync();
     __syncthreads();
@@ -543,8 +633,7 @@ rfsn_status launch(const CUtensorMap* maps, const PrefillParams& p, cudaStream_t
     const size_t smem = sizeof(Smem);
     auto kern = prefill_attn_kernel<T>;
     RFSN_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    const int ppc = BM / p.groups_per_kv;
-    dim3 grid((p.q_len + ppc - 1) / ppc, p.batch * p.kv_heads);
+    dim3 grid(p.nqb, p.batch * p.kv_heads, p.splits);
     kern<<<grid, NTHREADS, smem, stream>>>(maps[0], maps[1], maps[2], maps[3], p);
     RFSN_CUDA(cudaGetLastError());
     note_launch();

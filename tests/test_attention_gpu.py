@@ -204,3 +204,16 @@ def test_tensor_core_prefill_peaky_scores():
     rng = np.random.default_rng(83)
     q = (rng.standard_normal((1, 8, 128, 128)) * 6.0).astype(np.float32)
     _check(lay, q, lay.total_tokens - 128)
+
+
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
+@pytest.mark.parametrize("q_len,blocks,hot", [
+    (1280, [1000] * 5, 1024),  # 160 (query block, KV head) units -> 2 key-range splits per unit
+    (320, [1000] * 6, 512),    # 40 units over a long context -> 3 splits
+])
+def test_tensor_core_prefill_key_range_splits(dtype, q_len, blocks, hot):
+    # few query blocks over a long context: each block's key stream is split over
+    # several CTAs and the last one merges their (output, LSE) partials
+    lay = make_layout(dtype, 1, 4, 128, blocks, hot, hot, 7, seed=84)
+    q = _q(84, 1, 16, q_len, 128)
+    _check(lay, q, lay.total_tokens - q_len)
