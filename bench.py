@@ -270,7 +270,7 @@ def e2e_throughput(cache, w, world, owns_hot, steps, calls_per_step, peers=None)
 
     from rfsn_b200 import _native as native
     from rfsn_b200.layer import GraphedDecodeStep
-    from rfsn_b200.sharded import sharded_decode_step
+    from rfsn_b200.sharded import GraphedShardedDecodeStep, sharded_decode_step
 
     dt = cache.dtype
     H, Hkv, D = w["q_heads"], w["kv_heads"], w["head_dim"]
@@ -289,10 +289,15 @@ def e2e_throughput(cache, w, world, owns_hot, steps, calls_per_step, peers=None)
         pos = int(t.item())
 
     graphed = None
-    if world == 1:
-        # one graph replay per call: H2D of the token's q/k/v, RoPE + append,
-        # paged attention, D2H of the output (rfsn_b200.layer.GraphedDecodeStep)
-        graphed = GraphedDecodeStep(cache, H)
+    if world == 1 or peers is not None:
+        # one graph replay per call: H2D of the token's q (and k/v on the hot-window
+        # owner), RoPE + append, paged attention (merged over NVLink when sharded),
+        # D2H of the output (rfsn_b200.layer.GraphedDecodeStep /
+        # rfsn_b200.sharded.GraphedShardedDecodeStep)
+        if world == 1:
+            graphed = GraphedDecodeStep(cache, H)
+        else:
+            graphed = GraphedShardedDecodeStep(cache, H, owns_hot=owns_hot, peers=peers)
         graphed.q_host.copy_(q_h)
         graphed.k_host.copy_(k_h)
         graphed.v_host.copy_(v_h)
@@ -324,7 +329,10 @@ def e2e_throughput(cache, w, world, owns_hot, steps, calls_per_step, peers=None)
     if graphed is not None:  # kernels replayed inside the graph are not host launches
         launches += graphed.graph_kernels * (graphed.replays - replays0)
     barrier(world)
-    h2d = q_h.numel() * q_h.element_size() + (k_h.numel() * k_h.element_size() * 2 if owns_hot else 0)
+    if graphed is not None:  # the replay copies the whole packed staging buffer (step state + q/k/v)
+        h2d = graphed.stage_host.numel() * graphed.stage_host.element_size()
+    else:
+        h2d = q_h.numel() * q_h.element_size() + (k_h.numel() * k_h.element_size() * 2 if owns_hot else 0)
     d2h = out_h.numel() * out_h.element_size()
     return elapsed, n, launches, h2d, d2h
 
@@ -436,6 +444,10 @@ def run_ours(args, w):
             traffic = json.loads(prof.read_text()).get("dram_bytes_per_launch")
         except Exception:
             traffic = None
+    if traffic is not None and world > 1:
+        # captured on the whole context on one GPU; a rank's launch reads its shard,
+        # and the traffic grows in proportion to the K/V bytes it walks
+        traffic = int(traffic * local_bytes / algorithmic_bytes(w, total_tokens))
 
     secondary = None
     prefill = None
@@ -501,7 +513,9 @@ def run_ours(args, w):
                 "d2h_bytes_per_step": d2h * e2e_calls,
                 "calls_per_step": e2e_calls,
                 "api": "rfsn_b200.layer.GraphedDecodeStep (host buffers in/out, one graph replay per call)"
-                if world == 1 else "rfsn_b200.sharded.sharded_decode_step",
+                if world == 1 else ("rfsn_b200.sharded.GraphedShardedDecodeStep (host buffers in/out, one graph "
+                                    "replay per call, merge over NVLink in the kernel)" if peers is not None
+                                    else "rfsn_b200.sharded.sharded_decode_step (NCCL merge)"),
             },
             "gpu_launches": launches,
             "e2e_gpu_launches": e_launches,

@@ -151,8 +151,9 @@ RFSN_API rfsn_status rfsn_rope_append(const void* q, const void* k, const void* 
 /* rfsn_rope_append with the position and ring write index read on the device
  * from step_state[RFSN_STEP_POS] and step_state[RFSN_STEP_WRITE_INDEX] when the
  * kernel runs (capturable once in a CUDA graph and replayed for every decode
- * step). No counterpart in the reference: it only moves two arguments of
- * layer.py:131-135 into device memory. */
+ * step). k and v may be NULL to rotate q alone. No counterpart in the
+ * reference: it only moves two arguments of layer.py:131-135 into device
+ * memory. */
 RFSN_API rfsn_status rfsn_rope_append_step(const void* q, const void* k, const void* v, int in_dtype,
                                            const float* inv_freq, const int32_t* step_state, int batch, int q_heads,
                                            int kv_heads, int len, int head_dim, float* q_out,

@@ -219,11 +219,16 @@ rfsn_status rfsn_rope_append_step(const void* q, const void* k, const void* v, i
                                   void* stream) {
     RFSN_CHECK_ARG(step_state != nullptr, "rfsn_rope_append_step: NULL step state");
     RFSN_CHECK_ARG(arena != nullptr, "rfsn_rope_append_step: NULL arena");
-    RFSN_CHECK_ARG(k != nullptr && v != nullptr, "rfsn_rope_append_step: k and v are required");
+    RFSN_CHECK_ARG((k != nullptr) == (v != nullptr), "rfsn_rope_append_step: k and v must both be given or both NULL");
+    if (k == nullptr) {  // rotate q alone (a shard that does not own the hot window)
+        RFSN_CHECK_ARG(q != nullptr && q_out != nullptr && inv_freq != nullptr,
+                       "rfsn_rope_append_step: rotating q alone needs q, q_out and inv_freq");
+        kv_heads = 0;
+    }
     RFSN_CHECK_ARG(valid_dtype(in_dtype) && in_dtype == arena->dtype,
                    "rfsn_rope_append_step: input dtype %d differs from cache dtype %d", in_dtype, arena->dtype);
-    RFSN_CHECK_ARG(batch > 0 && kv_heads > 0 && len > 0 && q_heads >= 0, "rfsn_rope_append_step: non-positive shape");
-    RFSN_CHECK_ARG(head_dim == arena->head_dim && batch * kv_heads == arena->groups,
+    RFSN_CHECK_ARG(batch > 0 && kv_heads >= 0 && len > 0 && q_heads >= 0, "rfsn_rope_append_step: non-positive shape");
+    RFSN_CHECK_ARG(head_dim == arena->head_dim && (k == nullptr || batch * kv_heads == arena->groups),
                    "rfsn_rope_append_step: shape does not match the arena");
     RFSN_CHECK_ARG(capacity > 0 && ring_row0 >= 0 && ring_row0 + capacity <= arena->rows,
                    "rfsn_rope_append_step: ring rows outside the arena");

@@ -20,7 +20,7 @@ __global__ void rope_append_kernel(const TIn* __restrict__ q, const TIn* __restr
     if (step_state != nullptr) {  // position and write slot chosen when the kernel runs
         pos0 = step_state[0];
         write_index = step_state[1];
-        if ((unsigned)write_index >= (unsigned)capacity) return;  // never write outside the ring
+        if (kv_heads > 0 && (unsigned)write_index >= (unsigned)capacity) return;  // never write outside the ring
     }
     const int half = head_dim >> 1;
     const long q_rows = (long)batch * q_heads * len;

@@ -172,3 +172,92 @@ def sharded_decode_step(cache: LayerKVCache, q: torch.Tensor, k: Optional[torch.
     else:
         out, lse = cache.attend(q_rot, pos, segments, want_lse=True)
     return merge_across_ranks(out, lse, group)
+
+
+class GraphedShardedDecodeStep:
+    """``sharded_decode_step`` with a peer group, host buffers in and out, as one
+    CUDA graph replay per token on every rank.
+
+    Fill ``q_host`` (and, on the hot-window owner, ``k_host`` / ``v_host``) and
+    call ``step(pos)`` on every rank for every token, in the same order. The
+    host runs this rank's cache bookkeeping (the owner's seal rule and append
+    counters, the segment walk) and writes the step state; the graph copies the
+    staging buffer in, applies RoPE (and the ring append on the owner), runs the
+    decode kernel that merges all ranks' parts over NVLink, and copies the
+    merged output back to ``out_host``. A rank captures its graph again when
+    its own page table or arena changes (a seal on the owner); the kernels'
+    call stamps live on the device, so replays and re-captures stay matched
+    across ranks. Needs bf16/f16 K/V, head_dim 128 and <= 4 query heads per KV
+    head."""
+
+    def __init__(self, cache: LayerKVCache, q_heads: int, *, owns_hot: bool, peers: PeerGroup) -> None:
+        from .layer import GraphedDecodeStep  # staging layout and capture helper
+
+        self.cache = cache
+        self.owns_hot = owns_hot
+        self.peers = peers
+        self._inner = GraphedDecodeStep(cache, q_heads)  # buffers, workspace, stream
+        self.q_host, self.k_host, self.v_host = self._inner.q_host, self._inner.k_host, self._inner.v_host
+        self.out_host = self._inner.out_host
+        self.stage_host = self._inner.stage_host  # what one replay copies in (step state + q/k/v)
+        self.graph: Optional[torch.cuda.CUDAGraph] = None
+        self.key = None
+        self.replays = self.captures = 0
+        self.graph_kernels = 0
+
+    def _body(self, segs) -> torch.Tensor:
+        from .cache import paged_attention
+
+        c, inner = self.cache, self._inner
+        inner.stage_dev.copy_(inner.stage_host, non_blocking=True)
+        B, H, L, D = inner.shape_q
+        q_rot = torch.empty(inner.shape_q, dtype=torch.float32, device=c.device)
+        native.check(
+            native.lib().rfsn_rope_append_step(
+                inner.q_dev.data_ptr(), inner.k_dev.data_ptr() if self.owns_hot else None,
+                inner.v_dev.data_ptr() if self.owns_hot else None, native.dtype_code(c.dtype),
+                c.inv_freq().data_ptr(), inner.state_dev.data_ptr(), B, H, c.num_kv_heads if self.owns_hot else 0, 1, D,
+                q_rot.data_ptr(), c.arena.handle, 0, c.config.hot_capacity, native.stream_ptr()),
+            "rfsn_rope_append_step",
+        )
+        out = paged_attention(c, q_rot, 0, segs, workspace=inner.workspace, step_state=inner.state_dev,
+                              peers=self.peers)
+        self.out_host.copy_(out, non_blocking=True)
+        return out
+
+    def step(self, pos: int) -> torch.Tensor:
+        from .layer import capture_graph
+
+        c, inner = self.cache, self._inner
+        if self.owns_hot:
+            c.evict_for_append(1)
+            write_index = c.hot_write_index
+            c._check_append(1)
+            c.hot_seq_len += 1
+        else:
+            write_index = 0
+        segs = c.get_attention_segments()
+        head, hlen, hstart = segs.hot_state if segs.hot_state is not None else (0, 0, c.hot_start)
+        st = inner.state_host
+        st[0], st[1], st[2], st[3], st[4] = pos, write_index, head, hlen, hstart
+        key = (c.arena.handle.value, c._arena_k.data_ptr(),
+               (segs.table[0].data_ptr(),) + tuple(segs.table[1:]) if segs.table is not None else None)
+        if key != self.key or self.graph is None:
+            # this token runs op by op on the side stream (it takes part in the peers'
+            # exchange for this call), then the graph is captured without running it
+            inner.stream.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(inner.stream):
+                self._body(segs)
+            torch.cuda.current_stream().wait_stream(inner.stream)
+            self.graph = None
+            before = native.launch_count()
+            self.graph = capture_graph(lambda: self._body(segs), inner.stream)
+            self.graph_kernels = native.launch_count() - before  # this library's kernels per replay
+            self.key = key
+            self.captures += 1
+            torch.cuda.current_stream().synchronize()
+            return self.out_host
+        self.graph.replay()
+        self.replays += 1
+        torch.cuda.current_stream().synchronize()
+        return self.out_host

@@ -269,3 +269,112 @@ def test_peer_merge_timeout_is_reported_and_context_survives():
     assert got[0].startswith("timeout:") and "the cross-GPU merge timed out" in got[0], got[0]
     assert got[0].endswith("finite=True"), got[0]
     assert got[1] == "no call", got[1]
+
+
+def test_graphed_sharded_step_with_a_peer_group_of_one_matches_attention_step():
+    """GraphedShardedDecodeStep on the hot-window owner of a one-rank peer group
+    (the in-kernel merge runs with a single part) against attention_step on a twin
+    cache, over enough tokens to seal blocks and re-capture."""
+    import torch
+
+    from rfsn_b200.layer import attention_step
+    from rfsn_b200.sharded import GraphedShardedDecodeStep, PeerGroup
+
+    q, k, v, total = _data()
+    with tempfile.TemporaryDirectory() as tmp:
+        dev = torch.device("cuda", 0)
+        a = _shard_cache(0, 1, k, v, dev, tmp + "/a")
+        b = _shard_cache(0, 1, k, v, dev, tmp + "/b")
+        peers = PeerGroup(HKV, D)
+        step = GraphedShardedDecodeStep(b, H, owns_hot=True, peers=peers)
+        gen = torch.Generator(device="cuda").manual_seed(5)
+        pos = a.hot_end
+        for i in range(1200):  # the 512-token ring seals 1000-token blocks
+            qq = torch.randn((1, H, 1, D), generator=gen, device="cuda").to(torch.bfloat16)
+            kk = torch.randn((1, HKV, 1, D), generator=gen, device="cuda").to(torch.bfloat16)
+            vv = torch.randn((1, HKV, 1, D), generator=gen, device="cuda").to(torch.bfloat16)
+            want = attention_step(qq, kk, vv, a, pos).cpu()
+            step.q_host.copy_(qq.cpu())
+            step.k_host.copy_(kk.cpu())
+            step.v_host.copy_(vv.cpu())
+            got = step.step(pos)
+            assert float((got - want).abs().max()) <= 1e-5, i
+            pos += 1
+        assert (a.hot_head_index, a.hot_seq_len, a.hot_start) == (b.hot_head_index, b.hot_seq_len, b.hot_start)
+        assert step.replays > 1000 and step.captures >= 2, (step.replays, step.captures)
+        step._inner.workspace.check()
+        peers.close()
+
+
+def _graphed_worker(rank, world, port, results, tokens):
+    """Each rank drives two copies of its shard with the same peer group: one
+    through sharded_decode_step (op by op), one through GraphedShardedDecodeStep
+    (one graph replay per token; the owner re-captures after each seal while the
+    other ranks keep replaying)."""
+    try:
+        import sys
+
+        root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+        sys.path[:0] = [root, os.path.join(root, "rfsn-mlx_b200"), os.path.join(root, "tests")]
+        import torch
+        import torch.distributed as dist
+
+        from rfsn_b200 import _native as native
+        from rfsn_b200.sharded import GraphedShardedDecodeStep, PeerGroup, sharded_decode_step
+
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                                device_id=torch.device("cuda", rank))
+        q, k, v, total = _data()
+        dev = torch.device("cuda", rank)
+        owner = rank == world - 1
+        with tempfile.TemporaryDirectory() as tmp:
+            eager = _shard_cache(rank, world, k, v, dev, tmp + "/e")
+            graphed = _shard_cache(rank, world, k, v, dev, tmp + "/g")
+            peers = PeerGroup(HKV, D)
+            step = GraphedShardedDecodeStep(graphed, H, owns_hot=owner, peers=peers)
+            gen = torch.Generator().manual_seed(9)
+            worst = 0.0
+            for i in range(tokens):
+                qq = torch.randn((1, H, 1, D), generator=gen).to(torch.bfloat16)
+                kk = torch.randn((1, HKV, 1, D), generator=gen).to(torch.bfloat16)
+                vv = torch.randn((1, HKV, 1, D), generator=gen).to(torch.bfloat16)
+                pos = total + i
+                want = sharded_decode_step(eager, qq.to(dev), kk.to(dev) if owner else None,
+                                           vv.to(dev) if owner else None, pos, owns_hot=owner, peers=peers).cpu()
+                step.q_host.copy_(qq)
+                if owner:
+                    step.k_host.copy_(kk)
+                    step.v_host.copy_(vv)
+                got = step.step(pos)
+                worst = max(worst, float((got - want).abs().max()))
+            native.default_workspace(dev).check()
+            step._inner.workspace.check()
+            peers.close()
+            results.put((rank, (worst, step.replays, step.captures)))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        results.put((rank, "crash: " + traceback.format_exc()))
+
+
+@pytest.mark.skipif("not __import__('torch').cuda.device_count() >= 2", reason="needs 2 GPUs")
+def test_graphed_sharded_step_two_gpus_matches_op_by_op():
+    world, tokens = 2, 1100  # the owner's 512-token ring seals twice
+    ctx = mp.get_context("spawn")
+    results = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_graphed_worker, args=(r, world, port, results, tokens)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(results.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=120)
+    for rank in range(world):
+        assert not isinstance(got[rank], str), got[rank]
+        worst, replays, captures = got[rank]
+        assert worst <= 1e-5, (rank, worst)
+        assert replays + captures == tokens
+    assert got[world - 1][2] >= 3  # owner: first token and one per seal
+    assert got[0][2] == 1  # the other rank's page table never changes
