@@ -211,38 +211,126 @@ __device__ __forceinline__ void peer_store_and_merge(const PeerParams& peer, con
     if (lse != nullptr && d4 == 0) lse[om.row(group, sl)] = W > 0.f ? M + logf(W) : -CUDART_INF_F;
 }
 
-constexpr int kMergeDepth = 24;  // independent loads in flight per thread in the split merge
+constexpr int kMergeDepth = 24;  // independent loads in flight per thread in the split merge (default)
 
+template <int kDepth = kMergeDepth>
 __device__ __forceinline__ void finish_splits(const WsView& ws, int counter_idx, int part_base, int split_stride,
                                               int splits, int slot0, int nslots, int head_dim, const OutMap& om,
                                               int bh, float* out, float* lse, int* flag, float* sbuf, int bar_id,
-                                              int nthreads, const PeerParams* peer = nullptr, int call = 0) {
+                                              int nthreads, const PeerParams* peer = nullptr, int call = 0,
+                                              float4* stage = nullptr, int stage_vec4 = 0) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = nthreads >> 5;
-    __threadfence();
+    // One release-acquire arrival per CTA after a CTA barrier (no per-thread
+    // fences): the barrier orders every thread's partial stores before thread
+    // 0's release, and the last CTA's acquire followed by the barrier orders
+    // the other CTAs' partials before its threads' loads.
     named_barrier_sync(bar_id, nthreads);
     if (splits > 1) {
         if (tid == 0) {
-            int prev = atomicAdd(&ws.counters[counter_idx], 1);
+            int prev = atom_add_acq_rel_gpu(&ws.counters[counter_idx], 1);
             *flag = (prev == splits - 1);
         }
         named_barrier_sync(bar_id, nthreads);
         if (!*flag) return;
-        __threadfence();
     }
-    // The merge is a chain of L2 round trips (arrival atomic, m/l, O). Each
-    // thread's first kMergeDepth partial-output vectors are requested now, so
-    // they travel while the weights are computed; the rest follow in chunks of
-    // kMergeDepth independent loads.
+    // The merge is a chain of L2 round trips (arrival atomic, m/l, O). Without
+    // a staging area each thread's first kDepth partial-output vectors are
+    // requested first, so they travel while the weights are computed; the rest
+    // follow in chunks of kDepth independent loads.
     const int d4n = head_dim >> 2;
     const bool vec4 = (head_dim & 3) == 0;
     const int items = vec4 ? nslots * d4n : 0;
     const size_t o_stride = (size_t)split_stride * d4n;
-    float4 ov[kMergeDepth];
+    // With a shared staging area large enough for every split's partial outputs
+    // (splits x items float4), they are all requested at once by cp.async: one
+    // round trip whatever the split count, no registers held.
+    // The group's m and l runs (splits x split_stride floats each, from
+    // part_base) travel in the same round trip as 16-byte chunks.
+    const int ml_vec4 = splits * split_stride / 4;
+    const bool aligned16 = ((reinterpret_cast<uintptr_t>(ws.m) | reinterpret_cast<uintptr_t>(ws.l) |
+                             reinterpret_cast<uintptr_t>(ws.o)) & 15) == 0;
+    const bool staged = stage != nullptr && vec4 && d4n == 32 && aligned16 && (split_stride & 3) == 0 && (part_base & 3) == 0 &&
+                        (size_t)splits * items + 2 * (size_t)ml_vec4 <= (size_t)stage_vec4;
+    float4* st_m = stage + (size_t)splits * items;
+    float4* st_l = st_m + ml_vec4;
+    float4 ov[kDepth];
+    if (staged) {
+        const float4* gm = reinterpret_cast<const float4*>(ws.m + part_base);
+        const float4* gl = reinterpret_cast<const float4*>(ws.l + part_base);
+        for (int i = tid; i < ml_vec4; i += nthreads) {
+            cp_async_16(st_m + i, gm + i);
+            cp_async_16(st_l + i, gl + i);
+        }
+        for (int idx = tid; idx < items; idx += nthreads) {
+            const int sl = idx / d4n, d4 = idx - sl * d4n;
+            const float4* src = reinterpret_cast<const float4*>(ws.o) + (size_t)(part_base + slot0 + sl) * d4n + d4;
+            float4* dst = stage + idx;
+#pragma unroll 4
+            for (int s = 0; s < splits; ++s, src += o_stride, dst += items) cp_async_16(dst, src);
+        }
+        cp_async_commit();
+        cp_async_wait_all();
+        named_barrier_sync(bar_id, nthreads);  // every thread's m/l chunks have landed
+        // One warp per query slot, lane j = output float4 j of the slot (head_dim
+        // 128): the slot's max and weight sum over the splits with the lanes
+        // across splits and shuffle reductions, the weights written back over
+        // m, then each lane's weighted sum of its column vector over the splits.
+        const uint32_t a_m = smem_u32(st_m), a_l = smem_u32(st_l), a_o = smem_u32(stage);
+        const uint32_t ml_step = 4u * split_stride, o_step = 16u * items;
+        constexpr int kB = 8;  // splits per batch: independent loads issued together
+        for (int sl = warp; sl < nslots; sl += nwarps) {
+            const int d4 = lane, idx = sl * d4n + d4;
+            const uint32_t am = a_m + 4u * (slot0 + sl), al = a_l + 4u * (slot0 + sl), ao = a_o + 16u * idx;
+            float M = -CUDART_INF_F;
+            for (int s = lane; s < splits; s += 32) M = fmaxf(M, lds_f32(am + s * ml_step));
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+            float L = 0.f;
+            for (int s = lane; s < splits; s += 32) {
+                const float w = (M == -CUDART_INF_F) ? 0.f : ex2_approx(lds_f32(am + s * ml_step) - M);
+                L += w * lds_f32(al + s * ml_step);
+                sts_f32(am + s * ml_step, w);
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+            __syncwarp();
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int s0 = 0; s0 < splits; s0 += kB) {
+                float c[kB];
+                float4 ob[kB];
+#pragma unroll
+                for (int u = 0; u < kB; ++u) {
+                    const bool in = s0 + u < splits;
+                    c[u] = in ? lds_f32(am + (s0 + u) * ml_step) : 0.f;
+                    ob[u] = in ? lds_f4(ao + (s0 + u) * o_step) : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+                for (int u = 0; u < kB; ++u) {
+                    acc.x += c[u] * ob[u].x;
+                    acc.y += c[u] * ob[u].y;
+                    acc.z += c[u] * ob[u].z;
+                    acc.w += c[u] * ob[u].w;
+                }
+            }
+            const float inv = 1.f / fmaxf(L, 1e-9f);
+            const float4 r = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+            const float my_lse = (L > 0.f) ? (M + log2f(L)) * 0.69314718055994531f : -CUDART_INF_F;
+            if (peer == nullptr) {
+                *reinterpret_cast<float4*>(out + om.row(bh, slot0 + sl) * head_dim + 4 * d4) = r;
+                if (lse != nullptr && d4 == 0) lse[om.row(bh, slot0 + sl)] = my_lse;
+            } else {
+                peer_store_and_merge(*peer, ws, call, bh, sl, d4, head_dim, r, my_lse, om, out, lse);
+            }
+        }
+        if (splits > 1 && tid == 0) ws.counters[counter_idx] = 0;
+        if (peer != nullptr && tid == 0) peer->calls[bh] = call;
+        return;
+    }
     if (tid < items) {
         const int sl = tid / d4n, d4 = tid - sl * d4n;
         const float4* base = reinterpret_cast<const float4*>(ws.o) + (size_t)(part_base + slot0 + sl) * d4n + d4;
 #pragma unroll
-        for (int u = 0; u < kMergeDepth; ++u) ov[u] = u < splits ? __ldcg(base + (size_t)u * o_stride)
+        for (int u = 0; u < kDepth; ++u) ov[u] = u < splits ? __ldcg(base + (size_t)u * o_stride)
                                                                  : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     float* wts = sbuf;                          // [nslots][splits] m_s, then weights
@@ -285,16 +373,16 @@ __device__ __forceinline__ void finish_splits(const WsView& ws, int counter_idx,
             const float4* base = reinterpret_cast<const float4*>(ws.o) +
                                  (size_t)(part_base + slot0 + sl) * d4n + d4;
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int s0 = 0; s0 < splits; s0 += kMergeDepth) {
+            for (int s0 = 0; s0 < splits; s0 += kDepth) {
                 if (idx != tid || s0 != 0) {  // the first chunk of the first item is already in flight
 #pragma unroll
-                    for (int u = 0; u < kMergeDepth; ++u) {
+                    for (int u = 0; u < kDepth; ++u) {
                         ov[u] = s0 + u < splits ? __ldcg(base + (size_t)(s0 + u) * o_stride)
                                                 : make_float4(0.f, 0.f, 0.f, 0.f);
                     }
                 }
 #pragma unroll
-                for (int u = 0; u < kMergeDepth; ++u) {
+                for (int u = 0; u < kDepth; ++u) {
                     const float c = s0 + u < splits ? w[s0 + u] : 0.f;
                     acc.x += c * ov[u].x;
                     acc.y += c * ov[u].y;

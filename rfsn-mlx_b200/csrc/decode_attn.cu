@@ -54,6 +54,10 @@ struct Smem {
     int call;  // cross-GPU merge: this call's stamp for the group
 };
 
+// K and V stage buffers are contiguous (k then v): the merge staging area in float4.
+template <int STAGES>
+constexpr int stage_vec4() { return STAGES * 2 * 2 * HALF_BYTES / 16; }
+
 template <typename T, int STAGES>
 __global__ void __launch_bounds__(NTHREADS, 2)
 paged_decode_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_constant__ CUtensorMap mapV64,
@@ -364,8 +368,11 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
     }
     // The split merge reuses red_o as scratch once every consumer thread is past
     // the reads above (finish_splits starts with a barrier).
+    // The K/V stages are idle now (every load issued was consumed or drained):
+    // the last CTA stages all splits' partial outputs there in one round trip.
     finish_splits(p.ws, bh, part_base, SLOTS, p.splits, 0, p.nslots, D, om, bh, p.out, p.lse, &sm.flag,
-                  &sm.red_o[0][0][0], 1, NCW * 32, p.peer.world > 0 ? &p.peer : nullptr, sm.call);
+                  &sm.red_o[0][0][0], 1, NCW * 32, p.peer.world > 0 ? &p.peer : nullptr, sm.call,
+                  reinterpret_cast<float4*>(&sm.k[0][0][0]), stage_vec4<STAGES>());
 }
 
 template <typename T, int STAGES>

@@ -556,12 +556,11 @@ prefill_attn_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
             }
             if (ch == 0) p.ws.m[prow] = (ok && lt > 0.f) ? (m + log2f(lt)) * 0.69314718055994531f : -CUDART_INF_F;
             if (!ok && tid == 0 && it > 0) atomicExch(p.ws.error, kDevErrTimeout);
-            __threadfence();
+            // release-acquire arrival by one thread between CTA barriers (as finish_splits)
             named_barrier_sync(3, SOFTMAX_THREADS);
-            if (tid == 0) sm.flag = atomicAdd(&p.ws.counters[unit], 1) == p.splits - 1;
+            if (tid == 0) sm.flag = atom_add_acq_rel_gpu(&p.ws.counters[unit], 1) == p.splits - 1;
             named_barrier_sync(3, SOFTMAX_THREADS);
             if (sm.flag) {
-                __threadfence();
                 const size_t base = unit * p.splits * BM + r;
                 float M = -CUDART_INF_F;
                 for (int s = 0; s < p.splits; ++s) M = fmaxf(M, __ldcg(p.ws.m + base + (size_t)s * BM));
