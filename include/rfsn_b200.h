@@ -151,13 +151,23 @@ RFSN_API rfsn_status rfsn_rope_append(const void* q, const void* k, const void* 
 /* rfsn_rope_append with the position and ring write index read on the device
  * from step_state[RFSN_STEP_POS] and step_state[RFSN_STEP_WRITE_INDEX] when the
  * kernel runs (capturable once in a CUDA graph and replayed for every decode
- * step). k and v may be NULL to rotate q alone. No counterpart in the
- * reference: it only moves two arguments of layer.py:131-135 into device
- * memory. */
+ * step). k and v may be NULL to rotate q alone. q, k, v and step_state may be
+ * page-locked host memory (read over the bus by the kernel; see
+ * rfsn_host_device_pointer). step_state_copy (device int32[RFSN_STEP_STATE_LEN],
+ * may be NULL) receives the step state, for a decode kernel that reads it from
+ * device memory. No counterpart in the reference: it only moves two arguments
+ * of layer.py:131-135 into device memory. */
 RFSN_API rfsn_status rfsn_rope_append_step(const void* q, const void* k, const void* v, int in_dtype,
-                                           const float* inv_freq, const int32_t* step_state, int batch, int q_heads,
-                                           int kv_heads, int len, int head_dim, float* q_out,
-                                           const rfsn_arena* arena, int ring_row0, int capacity, void* stream);
+                                           const float* inv_freq, const int32_t* step_state,
+                                           int32_t* step_state_copy, int batch, int q_heads, int kv_heads, int len,
+                                           int head_dim, float* q_out, const rfsn_arena* arena, int ring_row0,
+                                           int capacity, void* stream);
+
+/* Device address of page-locked host memory (the same value under unified
+ * addressing), for kernels that read their inputs or write their outputs
+ * across the bus instead of through copy operations. RFSN_ERR_INVALID_ARG when
+ * host_ptr is not page-locked memory mapped for the current device. */
+RFSN_API rfsn_status rfsn_host_device_pointer(const void* host_ptr, void** device_ptr);
 
 /* ------------------------------------------------------------------------
  * Copy rows inside an arena (both K and V, every batch*kv head).

@@ -214,9 +214,9 @@ rfsn_status rfsn_rope_append(const void* q, const void* k, const void* v, int in
 }
 
 rfsn_status rfsn_rope_append_step(const void* q, const void* k, const void* v, int in_dtype, const float* inv_freq,
-                                  const int32_t* step_state, int batch, int q_heads, int kv_heads, int len,
-                                  int head_dim, float* q_out, const rfsn_arena* arena, int ring_row0, int capacity,
-                                  void* stream) {
+                                  const int32_t* step_state, int32_t* step_state_copy, int batch, int q_heads,
+                                  int kv_heads, int len, int head_dim, float* q_out, const rfsn_arena* arena,
+                                  int ring_row0, int capacity, void* stream) {
     RFSN_CHECK_ARG(step_state != nullptr, "rfsn_rope_append_step: NULL step state");
     RFSN_CHECK_ARG(arena != nullptr, "rfsn_rope_append_step: NULL arena");
     RFSN_CHECK_ARG((k != nullptr) == (v != nullptr), "rfsn_rope_append_step: k and v must both be given or both NULL");
@@ -239,7 +239,22 @@ rfsn_status rfsn_rope_append_step(const void* q, const void* k, const void* v, i
     const int qh = (inv_freq != nullptr && q != nullptr) ? q_heads : 0;
     return rope_append_launch(in_dtype, q, k, v, inv_freq, 0, batch, qh, kv_heads, len, head_dim, q_out, arena->k,
                               arena->v, arena->rows, ring_row0, capacity, 0, static_cast<cudaStream_t>(stream),
-                              step_state);
+                              step_state, step_state_copy);
+}
+
+rfsn_status rfsn_host_device_pointer(const void* host_ptr, void** device_ptr) {
+    RFSN_CHECK_ARG(host_ptr != nullptr && device_ptr != nullptr, "rfsn_host_device_pointer: NULL pointer");
+    *device_ptr = nullptr;
+    cudaPointerAttributes attr;
+    if (cudaPointerGetAttributes(&attr, host_ptr) != cudaSuccess) {
+        cudaGetLastError();
+        set_error("rfsn_host_device_pointer: not memory known to CUDA");
+        return RFSN_ERR_INVALID_ARG;
+    }
+    RFSN_CHECK_ARG(attr.type == cudaMemoryTypeHost && attr.devicePointer != nullptr,
+                   "rfsn_host_device_pointer: not page-locked host memory mapped for the device");
+    *device_ptr = attr.devicePointer;
+    return RFSN_OK;
 }
 
 rfsn_status rfsn_arena_copy_rows(const rfsn_arena* arena, int src_row0, int src_offset, int src_wrap, int dst_row0,
@@ -359,6 +374,10 @@ rfsn_status check_common(const float* q, int batch, int q_heads, int kv_heads, i
     RFSN_CHECK_ARG(batch > 0 && q_heads > 0 && kv_heads > 0 && q_len > 0, "attention: non-positive shape");
     RFSN_CHECK_ARG(q_heads % kv_heads == 0, "num_heads (%d) must be divisible by num_kv_heads (%d)", q_heads, kv_heads);
     RFSN_CHECK_ARG(head_dim > 0 && head_dim <= 256, "attention: head_dim %d outside [1, 256]", head_dim);
+    // the kernels store output rows as float4 when head_dim allows it
+    RFSN_CHECK_ARG(head_dim % 4 != 0 || reinterpret_cast<uintptr_t>(out) % 16 == 0,
+                   "attention: out must be 16-byte aligned");
+    RFSN_CHECK_ARG(reinterpret_cast<uintptr_t>(workspace) % 16 == 0, "attention: workspace must be 16-byte aligned");
     a->batch = batch;
     a->q_heads = q_heads;
     a->kv_heads = kv_heads;

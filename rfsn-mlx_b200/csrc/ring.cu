@@ -16,7 +16,10 @@ __global__ void rope_append_kernel(const TIn* __restrict__ q, const TIn* __restr
                                    const float* __restrict__ inv_freq, int pos0, int batch, int q_heads, int kv_heads,
                                    int len, int head_dim, float* __restrict__ q_out, TCache* __restrict__ ak,
                                    TCache* __restrict__ av, int rows, int ring_row0, int capacity, int write_index,
-                                   const int* __restrict__ step_state) {
+                                   const int* __restrict__ step_state, int* __restrict__ step_state_copy) {
+    if (step_state_copy != nullptr && blockIdx.x == 0 && threadIdx.x < RFSN_STEP_STATE_LEN) {
+        step_state_copy[threadIdx.x] = step_state[threadIdx.x];  // for the decode kernel that follows
+    }
     if (step_state != nullptr) {  // position and write slot chosen when the kernel runs
         pos0 = step_state[0];
         write_index = step_state[1];
@@ -91,7 +94,7 @@ __global__ void copy_rows_kernel(uint8_t* __restrict__ ak, uint8_t* __restrict__
 rfsn_status rope_append_launch(int dtype, const void* q, const void* k, const void* v, const float* inv_freq, int pos0,
                                int batch, int q_heads, int kv_heads, int len, int head_dim, float* q_out, void* ak,
                                void* av, int rows, int ring_row0, int capacity, int write_index, cudaStream_t stream,
-                               const int* step_state) {
+                               const int* step_state, int* step_state_copy) {
     const long total = ((long)batch * (q_heads + kv_heads) * len) * (head_dim / 2);
     const int threads = 256;
     long blocks = (total + threads - 1) / threads;
@@ -101,7 +104,7 @@ rfsn_status rope_append_launch(int dtype, const void* q, const void* k, const vo
     ring::rope_append_kernel<T, T><<<(unsigned)blocks, threads, 0, stream>>>(                                   \
         static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(v), inv_freq, pos0, batch,    \
         q_heads, kv_heads, len, head_dim, q_out, static_cast<T*>(ak), static_cast<T*>(av), rows, ring_row0,     \
-        capacity, write_index, step_state)
+        capacity, write_index, step_state, step_state_copy)
     if (dtype == RFSN_F32) {
         RFSN_ROPE_LAUNCH(float);
     } else if (dtype == RFSN_F16) {

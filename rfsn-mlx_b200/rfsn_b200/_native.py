@@ -64,6 +64,7 @@ EXPORTED_SYMBOLS = (
     "rfsn_peer_group_set_timeout",
     "rfsn_peer_group_destroy",
     "rfsn_paged_attention_peer",
+    "rfsn_host_device_pointer",
 )
 
 
@@ -140,7 +141,8 @@ def load_library() -> ctypes.CDLL:
         "rfsn_arena_create": (i32, [vp, vp, i32, i32, i32, i32, ctypes.POINTER(vp)]),
         "rfsn_arena_destroy": (i32, [vp]),
         "rfsn_rope_append": (i32, [vp, vp, vp, i32, vp, i32, i32, i32, i32, i32, i32, vp, vp, i32, i32, i32, vp]),
-        "rfsn_rope_append_step": (i32, [vp, vp, vp, i32, vp, vp, i32, i32, i32, i32, i32, vp, vp, i32, i32, vp]),
+        "rfsn_rope_append_step": (i32, [vp, vp, vp, i32, vp, vp, vp, i32, i32, i32, i32, i32, vp, vp, i32, i32, vp]),
+        "rfsn_host_device_pointer": (i32, [vp, ctypes.POINTER(ctypes.c_void_p)]),
         "rfsn_arena_copy_rows": (i32, [vp, i32, i32, i32, i32, i32, vp]),
         "rfsn_block_upload": (i32, [vp, i32, i32, vp, vp, vp, vp]),
         "rfsn_block_download": (i32, [vp, i32, i32, vp, vp, vp, vp]),
@@ -228,6 +230,19 @@ def stream_ptr(stream: Optional[torch.cuda.Stream] = None) -> int:
     if _raw_current_stream is not None and _current_device is not None:
         return int(_raw_current_stream(_current_device()))
     return int(torch.cuda.current_stream().cuda_stream)
+
+
+def host_device_pointer(t: torch.Tensor) -> int:
+    """Device address of a pinned CPU tensor's data, for kernels that read or
+    write it across the bus; raises ValueError when it is not page-locked
+    memory mapped for the current device."""
+    if t.device.type != "cpu" or not t.is_pinned():
+        raise ValueError("expected a pinned CPU tensor")
+    out = ctypes.c_void_p()
+    status = lib().rfsn_host_device_pointer(t.data_ptr(), ctypes.byref(out))
+    if status != RFSN_OK or not out.value:
+        raise ValueError(f"pinned tensor is not mapped for the device: {last_error()}")
+    return int(out.value)
 
 
 def dtype_code(dtype: torch.dtype) -> int:

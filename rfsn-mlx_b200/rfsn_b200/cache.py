@@ -843,7 +843,8 @@ class LayerKVCache:
 
 def paged_attention(cache: LayerKVCache, q: torch.Tensor, q_start_pos: int, segments: PagedSegments,
                     *, want_lse: bool = False, max_splits: int = 0, workspace: Optional[native.Workspace] = None,
-                    peers: Optional[Any] = None, step_state: Optional[torch.Tensor] = None):
+                    peers: Optional[Any] = None, step_state: Optional[torch.Tensor] = None,
+                    out: Optional[torch.Tensor] = None):
     """Exact attention of q over a layer's page table + hot window.
 
     With ``peers`` (a ``sharded.PeerGroup``) the kernel also merges the
@@ -854,14 +855,29 @@ def paged_attention(cache: LayerKVCache, q: torch.Tensor, q_start_pos: int, segm
     With ``step_state`` (device int32[8], ``_native.STEP_*``) the query position
     and the hot window are read from device memory when the kernel runs, so a
     captured CUDA graph of the call stays valid while the ring advances (the
-    page table is still captured by value)."""
+    page table is still captured by value).
+
+    ``out`` (float32 [B, H, Lq, D], contiguous) receives the result instead of
+    a new tensor: a tensor on the cache's device, or a pinned CPU tensor that
+    the kernel writes across the bus (no separate copy back)."""
     if len(segments) == 0 and peers is None:
         raise RuntimeError("run_segmented_attention requires at least one KV segment")
     if q.dim() != 4 or q.shape[0] != cache.batch_size or q.shape[3] != cache.config.head_dim:
         raise ValueError(f"q must be [batch={cache.batch_size}, heads, q_len, head_dim={cache.config.head_dim}]")
     qf = _as(q, cache.device, torch.float32)
     B, H, Lq, D = (int(x) for x in qf.shape)
-    out = torch.empty((B, H, Lq, D), dtype=torch.float32, device=cache.device)
+    if out is None:
+        out = torch.empty((B, H, Lq, D), dtype=torch.float32, device=cache.device)
+        out_ptr = out.data_ptr()
+    else:
+        if out.dtype != torch.float32 or tuple(out.shape) != (B, H, Lq, D) or not out.is_contiguous():
+            raise ValueError(f"out must be a contiguous float32 tensor of shape {(B, H, Lq, D)}")
+        if out.device.type == "cpu":
+            out_ptr = native.host_device_pointer(out)
+        elif out.device == cache.device:
+            out_ptr = out.data_ptr()
+        else:
+            raise ValueError(f"out must be on {cache.device} or pinned host memory")
     lse = torch.empty((B, H, Lq), dtype=torch.float32, device=cache.device) if want_lse else None
     if segments.table is not None:
         table_dev, n_blocks, toks, tiles = segments.table
@@ -884,7 +900,7 @@ def paged_attention(cache: LayerKVCache, q: torch.Tensor, q_start_pos: int, segm
         native.check(
             native.lib().rfsn_paged_attention_peer(
                 cache.arena.handle, qf.data_ptr(), B, H, cache.num_kv_heads, Lq, int(q_start_pos),
-                native.ctypes.byref(table), native.ctypes.byref(hot), peers.handle, out.data_ptr(),
+                native.ctypes.byref(table), native.ctypes.byref(hot), peers.handle, out_ptr,
                 lse.data_ptr() if lse is not None else None, buf.data_ptr(), buf.numel(), max_splits,
                 native.stream_ptr(),
             ),
@@ -894,7 +910,7 @@ def paged_attention(cache: LayerKVCache, q: torch.Tensor, q_start_pos: int, segm
     native.check(
         native.lib().rfsn_paged_attention(
             cache.arena.handle, qf.data_ptr(), B, H, cache.num_kv_heads, Lq, int(q_start_pos),
-            native.ctypes.byref(table), native.ctypes.byref(hot), out.data_ptr(),
+            native.ctypes.byref(table), native.ctypes.byref(hot), out_ptr,
             lse.data_ptr() if lse is not None else None, buf.data_ptr(), buf.numel(), max_splits,
             native.stream_ptr(),
         ),

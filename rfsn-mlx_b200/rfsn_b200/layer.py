@@ -72,11 +72,12 @@ class GraphedDecodeStep:
     Fill ``q_host`` [B, H, 1, D], ``k_host`` / ``v_host`` [B, Hkv, 1, D]
     (pinned, cache dtype) and call ``step(pos)``: the host runs the cache
     bookkeeping of ``attention_step`` (seal rule, append counters, prefetch
-    hook, segment walk), writes the step state, and replays a graph holding
-    one host-to-device copy (step state, q, k and v share one pinned staging
-    buffer), the fused RoPE/append and the paged decode kernel reading that
-    state, and the copy of the float32 output back to ``out_host``, which is
-    returned after the step completes. The graph is captured again when the
+    hook, segment walk), writes the step state, and replays a graph of two
+    kernels: the fused RoPE/append reads the step state, q, k and v straight
+    from the pinned staging buffer across the bus (no copy operation) and
+    leaves a device copy of the state, and the paged decode kernel reads that
+    state and writes the float32 output straight into the pinned
+    ``out_host``, which is returned after the step completes. The graph is captured again when the
     page table or the arena changes; when archived blocks are cold or a
     prefetch is in flight the step runs ``attention_step`` op by op instead.
     Needs bf16/f16 K/V, head_dim 128 and <= 4 query heads per KV head (the
@@ -99,7 +100,6 @@ class GraphedDecodeStep:
         n_kv = align(B * Hkv * D * es)
         total = n_state + n_q + 2 * n_kv
         self.stage_host = torch.zeros(total, dtype=torch.uint8).pin_memory()
-        self.stage_dev = torch.zeros(total, dtype=torch.uint8, device=dev)
 
         def views(buf):
             st = buf[:4 * native.STEP_STATE_LEN].view(torch.int32)
@@ -112,8 +112,13 @@ class GraphedDecodeStep:
             return st, q, k, v
 
         self.state_host, self.q_host, self.k_host, self.v_host = views(self.stage_host)
-        self.state_dev, self.q_dev, self.k_dev, self.v_dev = views(self.stage_dev)
+        self._state_np = self.state_host.numpy()  # element writes without torch indexing
+        self.state_dev = torch.zeros(native.STEP_STATE_LEN, dtype=torch.int32, device=dev)
         self.out_host = torch.zeros(self.shape_q, dtype=torch.float32).pin_memory()
+        # device addresses of the pinned buffers (the kernels read and write them across the bus)
+        base = native.host_device_pointer(self.stage_host) if self.supported else 0
+        self._dptr_state, self._dptr_q = base, base + n_state
+        self._dptr_k, self._dptr_v = base + n_state + n_q, base + n_state + n_q + n_kv
         self.workspace = native.Workspace(dev)
         self.workspace.get(native.workspace_bytes(B, q_heads, Hkv, 1, D, 0))
         self.stream = torch.cuda.Stream(device=dev)
@@ -131,19 +136,17 @@ class GraphedDecodeStep:
         from .cache import paged_attention
 
         c = self.cache
-        self.stage_dev.copy_(self.stage_host, non_blocking=True)
         B, H, L, D = self.shape_q
         q_rot = torch.empty(self.shape_q, dtype=torch.float32, device=c.device)
         native.check(
             native.lib().rfsn_rope_append_step(
-                self.q_dev.data_ptr(), self.k_dev.data_ptr(), self.v_dev.data_ptr(), native.dtype_code(c.dtype),
-                c.inv_freq().data_ptr(), self.state_dev.data_ptr(), B, H, c.num_kv_heads, 1, D, q_rot.data_ptr(),
+                self._dptr_q, self._dptr_k, self._dptr_v, native.dtype_code(c.dtype), c.inv_freq().data_ptr(),
+                self._dptr_state, self.state_dev.data_ptr(), B, H, c.num_kv_heads, 1, D, q_rot.data_ptr(),
                 c.arena.handle, 0, c.config.hot_capacity, native.stream_ptr()),
             "rfsn_rope_append_step",
         )
-        out = paged_attention(c, q_rot, 0, segs, workspace=self.workspace, step_state=self.state_dev)
-        self.out_host.copy_(out, non_blocking=True)
-        return out
+        return paged_attention(c, q_rot, 0, segs, workspace=self.workspace, step_state=self.state_dev,
+                               out=self.out_host)
 
     def step(self, pos: int) -> torch.Tensor:
         from . import _native as native
@@ -165,7 +168,7 @@ class GraphedDecodeStep:
         c.maybe_prefetch_for_decode(pos)
         segs = c.get_attention_segments()
         head, hlen, hstart = segs.hot_state
-        st = self.state_host
+        st = self._state_np
         st[0], st[1], st[2], st[3], st[4] = pos, write_index, head, hlen, hstart
         key = (c.arena.handle.value, c._arena_k.data_ptr(),
                (segs.table[0].data_ptr(),) + tuple(segs.table[1:]) if segs.table is not None else None)

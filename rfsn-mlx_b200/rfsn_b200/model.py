@@ -393,7 +393,7 @@ class _DecodeGraph:
         native.check(
             native.lib().rfsn_rope_append_step(
                 qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), native.dtype_code(lc.dtype), lc.inv_freq().data_ptr(),
-                self.state_dev.data_ptr(), B, H, lc.num_kv_heads, L, D, q_rot.data_ptr(), lc.arena.handle, 0,
+                self.state_dev.data_ptr(), None, B, H, lc.num_kv_heads, L, D, q_rot.data_ptr(), lc.arena.handle, 0,
                 lc.config.hot_capacity, native.stream_ptr()),
             "rfsn_rope_append_step",
         )

@@ -181,10 +181,10 @@ class GraphedShardedDecodeStep:
     Fill ``q_host`` (and, on the hot-window owner, ``k_host`` / ``v_host``) and
     call ``step(pos)`` on every rank for every token, in the same order. The
     host runs this rank's cache bookkeeping (the owner's seal rule and append
-    counters, the segment walk) and writes the step state; the graph copies the
-    staging buffer in, applies RoPE (and the ring append on the owner), runs the
-    decode kernel that merges all ranks' parts over NVLink, and copies the
-    merged output back to ``out_host``. A rank captures its graph again when
+    counters, the segment walk) and writes the step state; the graph applies
+    RoPE (and the ring append on the owner) reading the pinned staging buffer
+    across the bus, and runs the decode kernel that merges all ranks' parts
+    over NVLink and writes the merged output into the pinned ``out_host``. A rank captures its graph again when
     its own page table or arena changes (a seal on the owner); the kernels'
     call stamps live on the device, so replays and re-captures stay matched
     across ranks. Needs bf16/f16 K/V, head_dim 128 and <= 4 query heads per KV
@@ -209,21 +209,19 @@ class GraphedShardedDecodeStep:
         from .cache import paged_attention
 
         c, inner = self.cache, self._inner
-        inner.stage_dev.copy_(inner.stage_host, non_blocking=True)
         B, H, L, D = inner.shape_q
         q_rot = torch.empty(inner.shape_q, dtype=torch.float32, device=c.device)
+        # the kernels read the pinned staging buffer and write the pinned output across the bus
         native.check(
             native.lib().rfsn_rope_append_step(
-                inner.q_dev.data_ptr(), inner.k_dev.data_ptr() if self.owns_hot else None,
-                inner.v_dev.data_ptr() if self.owns_hot else None, native.dtype_code(c.dtype),
-                c.inv_freq().data_ptr(), inner.state_dev.data_ptr(), B, H, c.num_kv_heads if self.owns_hot else 0, 1, D,
-                q_rot.data_ptr(), c.arena.handle, 0, c.config.hot_capacity, native.stream_ptr()),
+                inner._dptr_q, inner._dptr_k if self.owns_hot else None, inner._dptr_v if self.owns_hot else None,
+                native.dtype_code(c.dtype), c.inv_freq().data_ptr(), inner._dptr_state, inner.state_dev.data_ptr(),
+                B, H, c.num_kv_heads if self.owns_hot else 0, 1, D, q_rot.data_ptr(), c.arena.handle, 0,
+                c.config.hot_capacity, native.stream_ptr()),
             "rfsn_rope_append_step",
         )
-        out = paged_attention(c, q_rot, 0, segs, workspace=inner.workspace, step_state=inner.state_dev,
-                              peers=self.peers)
-        self.out_host.copy_(out, non_blocking=True)
-        return out
+        return paged_attention(c, q_rot, 0, segs, workspace=inner.workspace, step_state=inner.state_dev,
+                               peers=self.peers, out=self.out_host)
 
     def step(self, pos: int) -> torch.Tensor:
         from .layer import capture_graph
@@ -238,7 +236,7 @@ class GraphedShardedDecodeStep:
             write_index = 0
         segs = c.get_attention_segments()
         head, hlen, hstart = segs.hot_state if segs.hot_state is not None else (0, 0, c.hot_start)
-        st = inner.state_host
+        st = inner._state_np
         st[0], st[1], st[2], st[3], st[4] = pos, write_index, head, hlen, hstart
         key = (c.arena.handle.value, c._arena_k.data_ptr(),
                (segs.table[0].data_ptr(),) + tuple(segs.table[1:]) if segs.table is not None else None)

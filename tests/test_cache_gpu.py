@@ -192,3 +192,37 @@ def test_graphed_decode_step_matches_attention_step():
             pos += 1
         assert step.replays > 250 and step.captures >= 3 and step.fallbacks == 0, (step.replays, step.captures)
         step.workspace.check()
+
+
+def test_paged_attention_into_given_output():
+    """paged_attention(out=...) writes the same result into a device tensor or
+    into pinned host memory (across the bus); other outputs are refused."""
+    from rfsn_b200 import LayerKVCache
+    from rfsn_b200 import _native as native
+    from rfsn_b200.cache import paged_attention
+
+    with tempfile.TemporaryDirectory() as tmp:
+        cfg = _cfg("bfloat16", 8, 2, 128, 256, 128, tmp)
+        c = LayerKVCache(cfg, 1, 8, 2, layer_id=0, session_id="out")
+        gen = torch.Generator(device="cuda").manual_seed(3)
+        k = torch.randn((1, 2, 256, 128), generator=gen, device="cuda").to(torch.bfloat16)
+        v = torch.randn((1, 2, 256, 128), generator=gen, device="cuda").to(torch.bfloat16)
+        for _ in range(2):
+            c.evict_for_append(256)
+            c.append_exact(k, v)
+        q = torch.randn((1, 8, 1, 128), generator=gen, device="cuda")
+        segs = c.get_attention_segments()
+        pos = c.hot_end - 1
+        want = paged_attention(c, q, pos, segs).cpu()
+        dev_out = torch.full((1, 8, 1, 128), float("nan"), device="cuda")
+        assert paged_attention(c, q, pos, segs, out=dev_out) is dev_out
+        pinned = torch.full((1, 8, 1, 128), float("nan")).pin_memory()
+        paged_attention(c, q, pos, segs, out=pinned)
+        torch.cuda.synchronize()
+        assert torch.equal(dev_out.cpu(), want) and torch.equal(pinned, want)
+        with pytest.raises(ValueError):
+            paged_attention(c, q, pos, segs, out=torch.zeros((1, 8, 1, 128)))  # pageable host memory
+        with pytest.raises(ValueError):
+            paged_attention(c, q, pos, segs, out=torch.zeros((1, 8, 2, 128), device="cuda"))
+        with pytest.raises(ValueError):
+            native.host_device_pointer(torch.zeros(4))
