@@ -70,28 +70,27 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
     const int split = blockIdx.x, bh = blockIdx.y;
     // Query position and hot window: launch arguments, or a device step state
     // (RFSN_STEP_*) read when the kernel runs. The state may be written by the
-    // work this launch overlaps, so it is read after the dependency wait; the
-    // tile ranges follow from it (the split count was fixed on the host for the
-    // largest window).
+    // work this launch overlaps, so it is read after the dependency wait, and
+    // the number of hot tiles follows from it; the split ranges were planned on
+    // the host for the largest window the ring holds, so a split's archived
+    // tiles are known before the wait and the producer streams them first.
     int q_pos0 = p.q_pos0, head = p.head, hlen = p.hlen, hstart = p.hstart;
-    int total_tiles = p.total_tiles, tiles_per_split = p.tiles_per_split;
-    if (p.dyn != nullptr) {
-        griddep_wait();
+    int total_tiles = p.total_tiles;
+    const int tiles_per_split = p.tiles_per_split;
+    const int tile0 = split * tiles_per_split;
+    auto read_state = [&](bool report) {
         q_pos0 = p.dyn[0];
         head = p.dyn[2];
         hlen = p.dyn[3];
         hstart = p.dyn[4];
         if (head < 0 || head >= p.capacity || hlen < 0 || hlen > p.capacity) {  // malformed: attend to no hot key
-            if (threadIdx.x == 0 && split == 0 && bh == 0) atomicExch(p.ws.error, kDevErrBadTable);
+            if (report) atomicExch(p.ws.error, kDevErrBadTable);
             head = 0;
             hlen = 0;
         }
         const int first = min(hlen, p.capacity - head);
         total_tiles = p.archived_tiles + (first + kTile - 1) / kTile + (hlen - first + kTile - 1) / kTile;
-        tiles_per_split = (total_tiles + p.splits - 1) / p.splits;
-    }
-    const int tile0 = split * tiles_per_split;
-    const int ntiles = min(tiles_per_split, total_tiles - tile0);
+    };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -105,6 +104,15 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
 
     if (warp == NCW) {
         // ---------------- producer: one elected lane issues all TMA loads ----------------
+        const bool dyn = p.dyn != nullptr;
+        bool have_state = !dyn;
+        if (dyn && tile0 >= p.archived_tiles) {  // the split starts in the hot window
+            griddep_wait();
+            read_state(false);
+            have_state = true;
+        }
+        // without the state, the split's archived tiles are the ones certainly there
+        int ntiles = min(tiles_per_split, (have_state ? total_tiles : p.archived_tiles) - tile0);
         PagedCursor cur;
         if (ntiles > 0) {
             if (lane == 0) {
@@ -116,12 +124,12 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
             cur.records = p.records;
             cur.n_blocks = p.n_blocks;
             cur.archived_tiles = p.archived_tiles;
-            cur.init_hot(p.ring_row0, p.capacity, head, hlen, hstart);
-            cur.seek_warp(tile0);
+            if (have_state) cur.init_hot(p.ring_row0, p.capacity, head, hlen, hstart);
+            cur.seek_warp(tile0);  // an archived tile when the hot window is not known yet
         }
         if (lane == 0 && ntiles > 0) {
             const int row_base = bh * p.rows;
-            bool waited = false;
+            bool waited = dyn && have_state;
             for (int it = 0; it < ntiles; ++it) {
                 const int s = it % STAGES;
                 if (it >= STAGES) {
@@ -163,6 +171,16 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
                         tma_load_2d(sm.v[s][1] + b * 1024, &mapV8, 64, grow + 8 * b, &sm.full[s]);
                     }
                 }
+                if (!have_state && tile0 + it + 1 >= p.archived_tiles) {
+                    // the next tile is a hot one: the window's rows and the split's
+                    // tile count come from the step state (before the cursor moves on)
+                    griddep_wait();
+                    waited = true;
+                    read_state(false);
+                    have_state = true;
+                    ntiles = min(tiles_per_split, total_tiles - tile0);
+                    cur.init_hot(p.ring_row0, p.capacity, head, hlen, hstart);
+                }
                 cur.advance();
             }
         }
@@ -180,6 +198,8 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
     // q (and the workspace written later) may come from the kernel this one
     // overlaps under programmatic dependent launch: wait for it first.
     griddep_wait();
+    if (p.dyn != nullptr) read_state(threadIdx.x == 0 && split == 0 && bh == 0);
+    const int ntiles = min(tiles_per_split, total_tiles - tile0);
     if (threadIdx.x == 0) sm.call = p.peer.world > 0 ? p.peer.calls[bh] + 1 : 0;
     uint32_t qf[8][2];
     {

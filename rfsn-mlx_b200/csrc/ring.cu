@@ -17,14 +17,11 @@ __global__ void rope_append_kernel(const TIn* __restrict__ q, const TIn* __restr
                                    int len, int head_dim, float* __restrict__ q_out, TCache* __restrict__ ak,
                                    TCache* __restrict__ av, int rows, int ring_row0, int capacity, int write_index,
                                    const int* __restrict__ step_state, int* __restrict__ step_state_copy) {
-    if (step_state_copy != nullptr && blockIdx.x == 0 && threadIdx.x < RFSN_STEP_STATE_LEN) {
-        step_state_copy[threadIdx.x] = step_state[threadIdx.x];  // for the decode kernel that follows
-    }
-    if (step_state != nullptr) {  // position and write slot chosen when the kernel runs
-        pos0 = step_state[0];
-        write_index = step_state[1];
-        if (kv_heads > 0 && (unsigned)write_index >= (unsigned)capacity) return;  // never write outside the ring
-    }
+    // A decode kernel launched after this one under programmatic dependent
+    // launch may start now: before its dependency wait it only reads archived
+    // arena rows, which this kernel never writes (it writes ring rows, q_out
+    // and the state copy, all read after that wait).
+    griddep_launch_dependents();
     const int half = head_dim >> 1;
     const long q_rows = (long)batch * q_heads * len;
     const long kv_rows = (long)batch * kv_heads * len;
@@ -35,17 +32,27 @@ __global__ void rope_append_kernel(const TIn* __restrict__ q, const TIn* __restr
         const bool is_q = r < q_rows;
         const long rr = is_q ? r : r - q_rows;
         const int l = (int)(rr % len);
-        float x1, x2;
+        // element loads first: with inputs in page-locked host memory they and
+        // the step-state loads below cross the bus together
+        float x1, x2, v1 = 0.f, v2 = 0.f;
         if (is_q) {
             x1 = to_f32<TIn>(q[rr * head_dim + j]);
             x2 = to_f32<TIn>(q[rr * head_dim + j + half]);
         } else {
             x1 = to_f32<TIn>(k[rr * head_dim + j]);
             x2 = to_f32<TIn>(k[rr * head_dim + j + half]);
+            v1 = to_f32<TIn>(v[rr * head_dim + j]);
+            v2 = to_f32<TIn>(v[rr * head_dim + j + half]);
+        }
+        int pos_s = pos0, wi = write_index;
+        if (step_state != nullptr) {  // position and write slot chosen when the kernel runs
+            pos_s = step_state[0];
+            wi = step_state[1];
+            if (kv_heads > 0 && (unsigned)wi >= (unsigned)capacity) continue;  // never write outside the ring
         }
         float o1 = x1, o2 = x2;
         if (inv_freq != nullptr) {
-            const float f = __fmul_rn((float)(pos0 + l), inv_freq[j]);
+            const float f = __fmul_rn((float)(pos_s + l), inv_freq[j]);
             const float c = cosf(f), s = sinf(f);
             o1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
             o2 = __fadd_rn(__fmul_rn(x1, s), __fmul_rn(x2, c));
@@ -58,13 +65,16 @@ __global__ void rope_append_kernel(const TIn* __restrict__ q, const TIn* __restr
         } else {
             // rr = (b * kv_heads + h) * len + l  ->  arena row of the ring slot
             const long bh = rr / len;
-            const int slot = (write_index + l) % capacity;
+            const int slot = (wi + l) % capacity;
             const long dst = (bh * rows + ring_row0 + slot) * head_dim;
             ak[dst + j] = from_f32<TCache>(o1);
             ak[dst + j + half] = from_f32<TCache>(o2);
-            av[dst + j] = from_f32<TCache>(to_f32<TIn>(v[rr * head_dim + j]));
-            av[dst + j + half] = from_f32<TCache>(to_f32<TIn>(v[rr * head_dim + j + half]));
+            av[dst + j] = from_f32<TCache>(v1);
+            av[dst + j + half] = from_f32<TCache>(v2);
         }
+    }
+    if (step_state_copy != nullptr && blockIdx.x == 0 && threadIdx.x < RFSN_STEP_STATE_LEN) {
+        step_state_copy[threadIdx.x] = step_state[threadIdx.x];  // for the decode kernel that follows
     }
 }
 
