@@ -97,7 +97,9 @@ typedef struct rfsn_hot_window {
     /* Optional device int32[RFSN_STEP_STATE_LEN] read by the kernel when it
      * runs (so one captured CUDA graph serves every decode step): the query
      * position replaces q_pos0 and the hot window replaces head_index / length
-     * / start_pos. NULL: the fields above are used. See RFSN_STEP_*. */
+     * / start_pos (a context that turns out empty gives zero output and -inf
+     * LSE instead of the argument error). NULL: the fields above are used.
+     * See RFSN_STEP_*. */
     const int32_t* step_state;
 } rfsn_hot_window;
 

@@ -431,7 +431,9 @@ rfsn_status rfsn::paged_attention_impl(const rfsn_arena* arena, const float* q, 
     const int first = hot->length < hot->capacity - hot->head_index ? hot->length : hot->capacity - hot->head_index;
     const int hot_tiles = (first + kTile - 1) / kTile + (hot->length - first + kTile - 1) / kTile;
     const int total_tiles = table->archived_tiles + hot_tiles;
-    if (total_tiles <= 0 && peer == nullptr) {
+    // With a device step state the window is only known when the kernel runs
+    // (an empty context then gives zero output and -inf LSE).
+    if (total_tiles <= 0 && peer == nullptr && hot->step_state == nullptr) {
         set_error("run_segmented_attention requires at least one KV segment");
         return RFSN_ERR_INVALID_ARG;
     }

@@ -119,8 +119,13 @@ def to_device_storage(x: np.ndarray, dtype: str):
     return torch.from_numpy(np.ascontiguousarray(x)).cuda()
 
 
-def run_paged(layout: PagedLayout, q: np.ndarray, q_pos0: int, *, max_splits: int = 0, want_lse: bool = True):
-    """Run rfsn_paged_attention on the layout through the C ABI; returns numpy out (and lse)."""
+def run_paged(layout: PagedLayout, q: np.ndarray, q_pos0: int, *, max_splits: int = 0, want_lse: bool = True,
+              step_state=None):
+    """Run rfsn_paged_attention on the layout through the C ABI; returns numpy out (and lse).
+
+    ``step_state`` (RFSN_STEP_* int32 values, or True for the layout's own
+    window and q_pos0) passes the query position and hot window through a
+    device step state instead of the call's arguments, which then carry zeros."""
     import torch
 
     from rfsn_b200 import _native as native
@@ -135,7 +140,16 @@ def run_paged(layout: PagedLayout, q: np.ndarray, q_pos0: int, *, max_splits: in
     lse = torch.empty((B, H, Lq), dtype=torch.float32, device="cuda")
     nblk = len(layout.block_lens)
     table = native.PageTableC(rec.data_ptr(), nblk, int(sum(layout.block_lens)), int(layout.records[nblk, 3]), 0)
-    hot = native.HotWindowC(0, layout.ring_cap, layout.hot_head, layout.hot_len, layout.hot_start)
+    if step_state is None:
+        hot = native.HotWindowC(0, layout.ring_cap, layout.hot_head, layout.hot_len, layout.hot_start)
+    else:
+        if step_state is True:
+            step_state = [q_pos0, 0, layout.hot_head, layout.hot_len, layout.hot_start, 0, 0, 0]
+        state = torch.tensor(list(step_state) + [0] * (native.STEP_STATE_LEN - len(step_state)), dtype=torch.int32,
+                             device="cuda")
+        # decoy window in the arguments: the kernel must take the state's
+        hot = native.HotWindowC(0, layout.ring_cap, 0, 1, 0, 0, state.data_ptr())
+        q_pos0 = 0
     nbytes = native.workspace_bytes(B, H, layout.kv_heads, Lq, D, max_splits)
     ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
     native.check(

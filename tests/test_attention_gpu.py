@@ -217,3 +217,35 @@ def test_tensor_core_prefill_key_range_splits(dtype, q_len, blocks, hot):
     lay = make_layout(dtype, 1, 4, 128, blocks, hot, hot, 7, seed=84)
     q = _q(84, 1, 16, q_len, 128)
     _check(lay, q, lay.total_tokens - q_len)
+
+
+@pytest.mark.parametrize("dtype,lens,cap,hot,head,G", [
+    ("bfloat16", [300, 257, 64, 1000], 4096, 100, 4050, 4),   # short window in a large ring, wrapped: empty splits
+    ("float16", [], 512, 500, 300, 4),                         # no archived block: every split starts in the ring
+    ("bfloat16", [1000] * 12 + [1024], 4096, 4096, 1234, 4),   # full wrapped ring behind archived blocks
+    ("bfloat16", [513, 64], 256, 1, 255, 2),                   # one hot token at the ring's last slot
+    ("float16", [129, 7], 96, 0, 17, 4),                       # empty window
+])
+def test_step_state_decode_matches_oracle(dtype, lens, cap, hot, head, G):
+    """The query position and hot window read from a device step state (the
+    graphed decode path: splits planned for the full ring, archived tiles
+    streamed before the state is read) give the oracle's result."""
+    lay = make_layout(dtype, 1, 8, 128, lens, cap, hot, head, seed=31)
+    q = _q(31, 1, 8 * G, 1, 128)
+    pos = lay.total_tokens - 1
+    ref, ref_lse = run_segmented_attention(q, lay.oracle_segments(), pos, return_lse=True, grouped=True)
+    out, lse = run_paged(lay, q, pos, step_state=True)
+    err = float(np.abs(out - ref).max())
+    assert err <= ATOL and err <= GUARD, err
+    np.testing.assert_allclose(lse, ref_lse, atol=1e-4, rtol=1e-5)
+    direct = run_paged(lay, q, pos, want_lse=False)
+    assert float(np.abs(out - direct).max()) <= 1e-6
+
+
+def test_step_state_outside_the_ring_is_reported():
+    """A step state whose hot window does not fit the ring is flagged as a
+    device error (the call attends to the archived blocks only)."""
+    lay = make_layout("bfloat16", 1, 8, 128, [300, 200], 256, 100, 10, seed=32)
+    q = _q(32, 1, 32, 1, 128)
+    with pytest.raises(RuntimeError, match="workspace"):
+        run_paged(lay, q, lay.total_tokens - 1, step_state=[lay.total_tokens - 1, 0, 256, 100, lay.hot_start])
