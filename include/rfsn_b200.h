@@ -165,6 +165,16 @@ RFSN_API rfsn_status rfsn_rope_append_step(const void* q, const void* k, const v
                                            int head_dim, float* q_out, const rfsn_arena* arena, int ring_row0,
                                            int capacity, void* stream);
 
+/* Launch plan of a tensor-core prefill call of this shape (rfsn_paged_attention
+ * with q_len >= 64, bf16/f16 K/V, head_dim 128): the units (query block of
+ * 128 / (q_heads / kv_heads) positions x KV head) are launched longest causal
+ * range first; the first *cta_units_whole run whole, each later one is split
+ * into *tail_splits key ranges whose last CTA merges them; *ctas CTAs in all.
+ * Host-only (uses the current device's SM count, 148 without a device). */
+RFSN_API rfsn_status rfsn_prefill_plan(int batch, int q_heads, int kv_heads, int q_len, int q_pos0,
+                                       int archived_tokens, int hot_start, int hot_length, int* cta_units_whole,
+                                       int* tail_splits, int* ctas);
+
 /* Device address of page-locked host memory (the same value under unified
  * addressing), for kernels that read their inputs or write their outputs
  * across the bus instead of through copy operations. RFSN_ERR_INVALID_ARG when

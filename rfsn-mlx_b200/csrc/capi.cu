@@ -1,8 +1,14 @@
 // C ABI entry points (include/rfsn_b200.h): argument checking, kernel
 // selection, split-KV sizing, TMA descriptor management and the small
 // utility kernels (row copies are in ring.cu, attention in *_attn.cu).
+#include <algorithm>
+#include <array>
 #include <atomic>
 #include <chrono>
+#include <functional>
+#include <map>
+#include <mutex>
+#include <vector>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -125,6 +131,91 @@ int generic_max_splits(int head_dim) {
     return m < kGenericMaxSplits ? m : kGenericMaxSplits;
 }
 
+// ---- launch plan of the tensor-core prefill ----
+// The kernel runs one CTA per SM; its units (query block, KV head) are
+// launched latest query blocks first. Costs are in 128-key tiles: a CTA costs
+// its tiles plus a fixed set-up / epilogue share, a split part also the
+// partial write and merge.
+constexpr double kPrefillCtaCost = 4.0;
+constexpr double kPrefillMergeCost = 3.0;
+constexpr int kPrefillMaxParts = 4;       // split parts per SM at most (bounds the workspace)
+
+struct PrefillPlan {
+    int full_units;   // units run whole (the first ones in launch order)
+    int tail_splits;  // key ranges of each later unit
+};
+
+// Makespan of greedy list scheduling (each CTA, in launch order, takes the SM
+// that frees first) when the units after the first `full` are split S ways.
+double prefill_makespan(const std::vector<double>& level_tiles, int groups, int full, int S, int sms,
+                        std::vector<double>& heap) {
+    heap.assign(sms, 0.0);  // all-zero: already a min-heap
+    double end = 0.0;
+    auto place = [&](double cost) {
+        std::pop_heap(heap.begin(), heap.end(), std::greater<double>());
+        heap.back() += cost;
+        end = std::max(end, heap.back());
+        std::push_heap(heap.begin(), heap.end(), std::greater<double>());
+    };
+    const int units = (int)level_tiles.size() * groups;
+    for (int u = 0; u < units; ++u) {
+        const double t = level_tiles[u / groups];
+        if (u < full) {
+            place(t + kPrefillCtaCost);
+        } else {
+            for (int s = 0; s < S; ++s) place(t / S + kPrefillCtaCost + kPrefillMergeCost);
+        }
+    }
+    return end;
+}
+
+// A launch's final wave is often partly empty (e.g. 512 units on 148 SMs:
+// 3.46 waves) while its units cost about the same, so the last SMs idle for
+// most of a unit. Candidates split the last `tail` units (the partial last
+// wave, that plus one more wave, or all units) into S = 2..4 key ranges; the
+// plan with the shortest estimated makespan is used when it beats the unsplit
+// launch by 3 %. Plans are cached per shape (every layer of a model repeats
+// them).
+PrefillPlan plan_prefill(int nqb, int groups, int ppc, int q_len, int q_pos0, int archived_tokens, int hstart,
+                         int hlen, int sms) {
+    static std::mutex mu;
+    static std::map<std::array<int, 9>, PrefillPlan> cache;
+    const std::array<int, 9> key = {nqb, groups, ppc, q_len, q_pos0 - hstart, archived_tokens, hlen, sms, 0};
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        auto it = cache.find(key);
+        if (it != cache.end()) return it->second;
+    }
+    std::vector<double> level(nqb);  // key tiles of launch level l (query block nqb - 1 - l)
+    for (int l = 0; l < nqb; ++l) {
+        const int qb = nqb - 1 - l;
+        const int qlast = q_pos0 + std::min((qb + 1) * ppc, q_len) - 1;
+        const int hot_keys = std::max(0, std::min(hlen, qlast - hstart + 1));
+        level[l] = (archived_tokens + hot_keys) / 128.0;
+    }
+    const int units = nqb * groups;
+    std::vector<double> heap;
+    PrefillPlan best{units, 1};
+    double best_t = 0.97 * prefill_makespan(level, groups, units, 1, sms, heap);
+    const int rem = units % sms;
+    for (int S = 2; S <= 4; ++S) {
+        for (int tail : {rem, rem + sms, units}) {
+            if (tail <= 0 || tail > units || tail > kMaxCounters || (long long)tail * S > (long long)kPrefillMaxParts * sms)
+                continue;
+            if (level[nqb - 1] / S < 8.0) continue;  // parts of the shortest units would be mostly overhead
+            const double t = prefill_makespan(level, groups, units - tail, S, sms, heap);
+            if (t < best_t) {
+                best_t = t;
+                best = {units - tail, S};
+            }
+        }
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    if (cache.size() > 1024) cache.clear();
+    cache[key] = best;
+    return best;
+}
+
 }  // namespace
 
 extern "C" {
@@ -242,6 +333,22 @@ rfsn_status rfsn_rope_append_step(const void* q, const void* k, const void* v, i
                               step_state, step_state_copy);
 }
 
+rfsn_status rfsn_prefill_plan(int batch, int q_heads, int kv_heads, int q_len, int q_pos0, int archived_tokens,
+                              int hot_start, int hot_length, int* cta_units_whole, int* tail_splits, int* ctas) {
+    RFSN_CHECK_ARG(cta_units_whole != nullptr && tail_splits != nullptr && ctas != nullptr, "rfsn_prefill_plan: NULL output");
+    RFSN_CHECK_ARG(batch > 0 && q_heads > 0 && kv_heads > 0 && q_len > 0 && q_heads % kv_heads == 0,
+                   "rfsn_prefill_plan: bad shape");
+    const int G = q_heads / kv_heads;
+    RFSN_CHECK_ARG(G <= 128, "rfsn_prefill_plan: %d query heads per KV head (max 128)", G);
+    const int ppc = 128 / G, nqb = (q_len + ppc - 1) / ppc, units = nqb * batch * kv_heads;
+    const PrefillPlan plan = plan_prefill(nqb, batch * kv_heads, ppc, q_len, q_pos0, archived_tokens, hot_start,
+                                          hot_length, sm_count_cached());
+    *cta_units_whole = plan.full_units;
+    *tail_splits = plan.tail_splits;
+    *ctas = plan.full_units + (units - plan.full_units) * plan.tail_splits;
+    return RFSN_OK;
+}
+
 rfsn_status rfsn_host_device_pointer(const void* host_ptr, void** device_ptr) {
     RFSN_CHECK_ARG(host_ptr != nullptr && device_ptr != nullptr, "rfsn_host_device_pointer: NULL pointer");
     *device_ptr = nullptr;
@@ -350,12 +457,30 @@ rfsn_status rfsn_attention_workspace_size(int batch, int q_heads, int kv_heads, 
     RFSN_CHECK_ARG(batch > 0 && q_heads > 0 && kv_heads > 0 && q_len > 0 && head_dim > 0,
                    "rfsn_attention_workspace_size: non-positive shape");
     RFSN_CHECK_ARG(q_heads % kv_heads == 0, "num_heads (%d) must be divisible by num_kv_heads (%d)", q_heads, kv_heads);
+    // The largest layout any kernel can choose for this shape: split counts
+    // follow from the SM count (at least 148 assumed, so a size computed
+    // without a device still serves a B200).
     const int G = q_heads / kv_heads;
     const int nslots = q_len * G;
     const int slots_ws = nslots < 4 ? 4 : nslots;
     const int qblocks = (nslots + 7) / 8;
-    const int splits = max_splits > 0 ? max_splits : kGenericMaxSplits;
-    *bytes = ws_layout(batch * kv_heads, qblocks, splits, slots_ws, head_dim).total;
+    const int groups = batch * kv_heads;
+    const int sms = std::max(sm_count_cached(), 148);
+    auto bound = [&](int cap, int target, int units) {
+        int s = std::max(1, target / std::max(units, 1));
+        if (max_splits > 0) s = std::min(s, max_splits);
+        return std::max(1, std::min(s, cap));
+    };
+    size_t need = ws_layout(groups, qblocks, bound(generic_max_splits(head_dim), sms * 4, groups * qblocks), slots_ws,
+                            head_dim).total;  // CUDA-core kernel
+    if (head_dim == 128 && nslots <= 4) {  // tensor-core decode kernel
+        need = std::max(need, ws_layout(groups, 1, bound(fast_max_splits(), sms * kFastCtasPerSm, groups), slots_ws,
+                                        128).total);
+    }
+    if (head_dim == 128 && q_len >= kPrefillMinRows) {  // tensor-core prefill: split parts
+        need = std::max(need, ws_layout(1, 1, kPrefillMaxParts * sms, 128, 128).total);
+    }
+    *bytes = need;
     return RFSN_OK;
 }
 
@@ -450,32 +575,19 @@ rfsn_status rfsn::paged_attention_impl(const rfsn_arena* arena, const float* q, 
         return RFSN_ERR_UNSUPPORTED;
     }
     if (use_prefill) {
-        // One CTA per (query block, KV head) streams the whole causal key range. When
-        // there are too few of them to keep the SMs busy (one CTA per SM; a short chunk
-        // over a long context), each query block's key stream is split into S even
-        // ranges and the last CTA of the block merges the results. With many units the
-        // causal spread of their lengths already fills the last wave and splitting
-        // only adds overhead (measured on the 2048-token chunks of a 32K prompt).
-        const int nqb = (q_len + 128 / a.G - 1) / (128 / a.G);
+        // One CTA per (query block, KV head) streams the whole causal key range; the
+        // units of a partly filled last wave (or of a launch too small for the SMs)
+        // may be split into key ranges merged by their last CTA (plan_prefill).
+        const int ppc = 128 / a.G;
+        const int nqb = (q_len + ppc - 1) / ppc;
         const int units = nqb * a.groups;
-        const int avg_tiles = (q_pos0 + q_len / 2) / 128;
-        auto wave_eff = [&](int n) { return (double)n / ((double)((n + sms - 1) / sms) * sms); };
-        int splits = 1;
-        double best = wave_eff(units);
-        if (best < 0.75) {
-            for (int cand = 2; cand <= 4; ++cand) {
-                if (avg_tiles / cand < 16 || units > kMaxCounters) break;
-                const double e = wave_eff(units * cand);
-                if (e > best + 0.05) {
-                    best = e;
-                    splits = cand;
-                }
-            }
-        }
-        WsLayout w = ws_layout(a.groups, 1, splits > 1 ? nqb * splits : 1, splits > 1 ? 128 : a.slots_ws, 128);
-        if (w.total > workspace_bytes && splits > 1) {
-            splits = 1;
-            w = ws_layout(a.groups, 1, 1, a.slots_ws, 128);
+        PrefillPlan plan = plan_prefill(nqb, a.groups, ppc, q_len, q_pos0, table->archived_tokens, hot->start_pos,
+                                        hot->length, sms);
+        const int parts = (units - plan.full_units) * plan.tail_splits;
+        WsLayout w = ws_layout(1, 1, plan.tail_splits > 1 ? parts : 1, 128, 128);
+        if (w.total > workspace_bytes && plan.tail_splits > 1) {  // a small workspace: run every unit whole
+            plan = {units, 1};
+            w = ws_layout(1, 1, 1, 128, 128);
         }
         if (w.total > workspace_bytes) {
             set_error("attention workspace too small: need %zu bytes, have %zu", w.total, workspace_bytes);
@@ -483,8 +595,9 @@ rfsn_status rfsn::paged_attention_impl(const rfsn_arena* arena, const float* q, 
         }
         PrefillParams pp;
         memset(&pp, 0, sizeof(pp));
-        pp.splits = splits;
         pp.nqb = nqb;
+        pp.full_units = plan.full_units;
+        pp.tail_splits = plan.tail_splits;
         pp.q = q;
         pp.out = out;
         pp.lse = lse;

@@ -48,8 +48,10 @@ struct PrefillParams {
     int rows;                 // arena rows per head
     int batch, q_heads, kv_heads, q_len, q_pos0, groups_per_kv;
     float qscale;             // 1/sqrt(D) * log2(e)
-    int splits, nqb;          // key-range splits per query block (grid z), query blocks (grid x)
-    WsView ws;                // error word; with splits > 1 also counters and partial (O, LSE)
+    int nqb;                  // query blocks per KV head
+    int full_units;           // units (query block, KV head) run whole, in launch order
+    int tail_splits;          // key ranges each later unit is split into (1: none)
+    WsView ws;                // error word; with split units also counters and partial (O, LSE)
 };
 
 namespace generic {

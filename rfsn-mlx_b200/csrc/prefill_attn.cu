@@ -205,14 +205,29 @@ prefill_attn_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = p.groups_per_kv;
     const int ppc = BM / G;                                   // chunk positions per CTA
-    const int qb = gridDim.x - 1 - blockIdx.x;                // longest (latest) rows first
-    const int bh = blockIdx.y;                                // b * kv_heads + kv head
+    // Work units (query block, KV head) in launch order: latest query blocks
+    // first (the longest causal key ranges), KV heads interleaved. The first
+    // full_units run whole; each later unit is split into tail_splits key
+    // ranges run by consecutive CTAs, and the last of them to finish merges the
+    // partial results (so the launch's final wave is evenly filled).
+    const int groups = p.batch * p.kv_heads;
+    int unit, split, nsplit;
+    if ((int)blockIdx.x < p.full_units) {
+        unit = blockIdx.x;
+        split = 0;
+        nsplit = 1;
+    } else {
+        const int j = blockIdx.x - p.full_units;
+        unit = p.full_units + j / p.tail_splits;
+        split = j % p.tail_splits;
+        nsplit = p.tail_splits;
+    }
+    const int tail_index = unit - p.full_units;               // counters and partials of split units
+    const int qb = p.nqb - 1 - unit / groups;
+    const int bh = unit % groups;                             // b * kv_heads + kv head
     const int b = bh / p.kv_heads, hk = bh % p.kv_heads;
     const int pos_base = qb * ppc;                            // first chunk position of the CTA
     const int qlast = p.q_pos0 + min(pos_base + ppc, p.q_len) - 1;  // causal limit of the CTA
-    // Key-range split: CTA z of a query block streams tiles [t0, t1) of its key
-    // stream (even shares); the last CTA to finish merges the partial results.
-    const int split = blockIdx.z;
 
     // ---- set-up: zero the K/V stages (rows past a ragged span end stay finite),
     //      barriers, TMEM ----
@@ -260,10 +275,10 @@ prefill_attn_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
             prefetch_tmap(&mapK64);
             prefetch_tmap(&mapK8);
             int t0 = 0, t1 = 1 << 30;
-            if (p.splits > 1) {
+            if (nsplit > 1) {  // this CTA streams tiles [t0, t1) of the unit's key stream (even shares)
                 const int ntile = count_tiles(p, qlast);
-                t0 = (int)((long long)split * ntile / p.splits);
-                t1 = (int)((long long)(split + 1) * ntile / p.splits);
+                t0 = (int)((long long)split * ntile / nsplit);
+                t1 = (int)((long long)(split + 1) * ntile / nsplit);
             }
             TileWalk walk;
             int it = 0, gi = -1, kpos0, row, nvalid;
@@ -305,10 +320,10 @@ prefill_attn_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
             prefetch_tmap(&mapV64);
             prefetch_tmap(&mapV8);
             int t0 = 0, t1 = 1 << 30;
-            if (p.splits > 1) {
+            if (nsplit > 1) {  // this CTA streams tiles [t0, t1) of the unit's key stream (even shares)
                 const int ntile = count_tiles(p, qlast);
-                t0 = (int)((long long)split * ntile / p.splits);
-                t1 = (int)((long long)(split + 1) * ntile / p.splits);
+                t0 = (int)((long long)split * ntile / nsplit);
+                t1 = (int)((long long)(split + 1) * ntile / nsplit);
             }
             TileWalk walk;
             int it = 0, gi = -1, kpos0, row, nvalid;
@@ -537,11 +552,10 @@ prefill_attn_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
         const float lt = ok ? l + sm.red[0][ch ^ 1][r] : 0.f;
         float* dst = p.out + (((size_t)b * p.q_heads + h) * p.q_len + (row_ok ? qrow : 0)) * D + 64 * ch;
         const float inv = (ok && lt > 0.f) ? 1.f / lt : 0.f;
-        if (p.splits > 1) {
+        if (nsplit > 1) {
             // this split's normalised output and natural-log LSE -> workspace; the last
-            // split CTA of the query block combines them (an empty range: LSE -inf)
-            const size_t unit = (size_t)bh * p.nqb + qb;
-            const size_t prow = (unit * p.splits + split) * BM + r;
+            // split CTA of the unit combines them (an empty range: LSE -inf)
+            const size_t prow = ((size_t)tail_index * nsplit + split) * BM + r;
             float* po = p.ws.o + prow * D + 64 * ch;
 #pragma unroll 1
             for (int cc = 0; cc < 2; ++cc) {
@@ -558,17 +572,17 @@ prefill_attn_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
             if (!ok && tid == 0 && it > 0) atomicExch(p.ws.error, kDevErrTimeout);
             // release-acquire arrival by one thread between CTA barriers (as finish_splits)
             named_barrier_sync(3, SOFTMAX_THREADS);
-            if (tid == 0) sm.flag = atom_add_acq_rel_gpu(&p.ws.counters[unit], 1) == p.splits - 1;
+            if (tid == 0) sm.flag = atom_add_acq_rel_gpu(&p.ws.counters[tail_index], 1) == nsplit - 1;
             named_barrier_sync(3, SOFTMAX_THREADS);
             if (sm.flag) {
-                const size_t base = unit * p.splits * BM + r;
+                const size_t base = (size_t)tail_index * nsplit * BM + r;
                 float M = -CUDART_INF_F;
-                for (int s = 0; s < p.splits; ++s) M = fmaxf(M, __ldcg(p.ws.m + base + (size_t)s * BM));
+                for (int s = 0; s < nsplit; ++s) M = fmaxf(M, __ldcg(p.ws.m + base + (size_t)s * BM));
                 float acc[64];
 #pragma unroll
                 for (int d = 0; d < 64; ++d) acc[d] = 0.f;
                 float L = 0.f;
-                for (int s = 0; s < p.splits; ++s) {
+                for (int s = 0; s < nsplit; ++s) {
                     const float ls = __ldcg(p.ws.m + base + (size_t)s * BM);
                     const float wgt = (M == -CUDART_INF_F) ? 0.f : exp2f((ls - M) * 1.4426950408889634f);
                     L += wgt;
@@ -594,7 +608,7 @@ prefill_attn_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
                             L > 0.f ? M + logf(L) : -CUDART_INF_F;
                     }
                 }
-                if (tid == 0) p.ws.counters[unit] = 0;  // ready for the next call
+                if (tid == 0) p.ws.counters[tail_index] = 0;  // ready for the next call
             }
         } else {
 #pragma unroll 1
@@ -632,7 +646,8 @@ rfsn_status launch(const CUtensorMap* maps, const PrefillParams& p, cudaStream_t
     const size_t smem = sizeof(Smem);
     auto kern = prefill_attn_kernel<T>;
     RFSN_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    dim3 grid(p.nqb, p.batch * p.kv_heads, p.splits);
+    const int units = p.nqb * p.batch * p.kv_heads;
+    dim3 grid(p.full_units + (units - p.full_units) * p.tail_splits);
     kern<<<grid, NTHREADS, smem, stream>>>(maps[0], maps[1], maps[2], maps[3], p);
     RFSN_CUDA(cudaGetLastError());
     note_launch();

@@ -65,6 +65,7 @@ EXPORTED_SYMBOLS = (
     "rfsn_peer_group_destroy",
     "rfsn_paged_attention_peer",
     "rfsn_host_device_pointer",
+    "rfsn_prefill_plan",
 )
 
 
@@ -143,6 +144,7 @@ def load_library() -> ctypes.CDLL:
         "rfsn_rope_append": (i32, [vp, vp, vp, i32, vp, i32, i32, i32, i32, i32, i32, vp, vp, i32, i32, i32, vp]),
         "rfsn_rope_append_step": (i32, [vp, vp, vp, i32, vp, vp, vp, i32, i32, i32, i32, i32, vp, vp, i32, i32, vp]),
         "rfsn_host_device_pointer": (i32, [vp, ctypes.POINTER(ctypes.c_void_p)]),
+        "rfsn_prefill_plan": (i32, [i32] * 8 + [ctypes.POINTER(ctypes.c_int)] * 3),
         "rfsn_arena_copy_rows": (i32, [vp, i32, i32, i32, i32, i32, vp]),
         "rfsn_block_upload": (i32, [vp, i32, i32, vp, vp, vp, vp]),
         "rfsn_block_download": (i32, [vp, i32, i32, vp, vp, vp, vp]),
@@ -243,6 +245,17 @@ def host_device_pointer(t: torch.Tensor) -> int:
     if status != RFSN_OK or not out.value:
         raise ValueError(f"pinned tensor is not mapped for the device: {last_error()}")
     return int(out.value)
+
+
+def prefill_plan(batch: int, q_heads: int, kv_heads: int, q_len: int, q_pos0: int, archived_tokens: int,
+                 hot_start: int, hot_length: int) -> tuple[int, int, int]:
+    """(units run whole, key-range splits of the later units, CTAs) of a
+    tensor-core prefill call of this shape (``rfsn_prefill_plan``)."""
+    whole, splits, ctas = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    check(load_library().rfsn_prefill_plan(batch, q_heads, kv_heads, q_len, q_pos0, archived_tokens, hot_start,
+                                           hot_length, ctypes.byref(whole), ctypes.byref(splits), ctypes.byref(ctas)),
+          "rfsn_prefill_plan")
+    return whole.value, splits.value, ctas.value
 
 
 def dtype_code(dtype: torch.dtype) -> int:

@@ -39,6 +39,35 @@ def test_workspace_size_is_host_only_and_validates():
         native.workspace_bytes(1, 30, 8, 1, 128)
 
 
+def test_workspace_size_follows_the_split_counts_the_kernels_choose():
+    # decode: at most 2 CTAs per SM of the tensor-core kernel or 4 of the CUDA-core
+    # one; a 2048-token prefill chunk: split parts of the tensor-core kernel
+    assert native.workspace_bytes(1, 32, 8, 1, 128) < 4 << 20
+    prefill = native.workspace_bytes(1, 32, 8, 2048, 128)
+    assert prefill >= 4 * 148 * 128 * 129 * 4 and prefill < 64 << 20
+    # an explicit split cap never asks for more
+    assert native.workspace_bytes(1, 32, 8, 1, 128, 8) <= native.workspace_bytes(1, 32, 8, 1, 128)
+
+
+def test_prefill_plan_fills_the_last_wave():
+    chunk = 2048
+    units = (chunk // 32) * 8  # 32 positions x 8 KV heads per unit
+    for c in range(16):  # 32K prompt in 2048-token chunks, 4096-token hot ring
+        nb = max(0, c - 1)
+        whole, splits, ctas = native.prefill_plan(1, 32, 8, chunk, c * chunk, nb * chunk, nb * chunk, min(c + 1, 2) * chunk)
+        assert 1 <= splits <= 4 and 0 <= whole <= units
+        assert ctas == whole + (units - whole) * splits
+        assert (units - whole) * splits <= 4 * 148 or splits == 1
+        if c >= 4:  # near-equal units: 3 full waves run whole, the 68 of the last wave in halves
+            assert (whole, splits) == (units - units % 148, 2), (c, whole, splits)
+    assert native.prefill_plan(1, 32, 8, chunk, 0, 0, 0, chunk)[1] == 1  # first chunk: short units, no split
+    # few units over a long context: every unit split
+    whole, splits, ctas = native.prefill_plan(1, 16, 4, 320, 6000 + 512 - 320, 6000, 6000, 512)
+    assert whole == 0 and splits > 1
+    with pytest.raises(ValueError):
+        native.prefill_plan(1, 30, 8, 64, 0, 0, 0, 64)
+
+
 def test_struct_layouts_match_header():
     assert ctypes.sizeof(native.PageTableC) == 24
     assert ctypes.sizeof(native.HotWindowC) == 32
