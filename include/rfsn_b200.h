@@ -112,7 +112,9 @@ typedef struct rfsn_hot_window {
 #define RFSN_STEP_STATE_LEN 8
 
 /* One K/V arena pair of a layer; holds the TMA descriptors the decode kernel
- * streams tiles with. Created once per cache layer. */
+ * streams tiles with. Created once per cache layer. The first arena created
+ * on a device also loads every kernel of the library there (none is then
+ * loaded lazily at its first launch, in the middle of a decode step). */
 typedef struct rfsn_arena rfsn_arena;
 
 RFSN_API rfsn_status rfsn_arena_create(void* k_arena,      /* device */

@@ -131,6 +131,19 @@ int generic_max_splits(int head_dim) {
     return m < kGenericMaxSplits ? m : kGenericMaxSplits;
 }
 
+// Every kernel of the library is loaded on a device when its first arena is
+// created, so no decode step pays a module load at a kernel's first launch.
+void preload_kernels_once(int dev) {
+    static std::atomic<bool> done[64];
+    if (dev < 0 || dev >= 64 || done[dev].exchange(true)) return;
+    preload_fast_kernels();
+    preload_generic_kernels();
+    preload_ring_kernels();
+    preload_merge_kernels();
+    preload_prefill_kernels();
+    cudaGetLastError();  // a kernel that cannot be loaded here reports the error at its launch
+}
+
 // ---- launch plan of the tensor-core prefill ----
 // The kernel runs one CTA per SM; its units (query block, KV head) are
 // launched latest query blocks first. Costs are in 128-key tiles: a CTA costs
@@ -251,6 +264,7 @@ rfsn_status rfsn_arena_create(void* k_arena, void* v_arena, int dtype, int batch
     a->rows = rows;
     a->head_dim = head_dim;
     cudaGetDevice(&a->device);
+    preload_kernels_once(a->device);
     a->has_tma = false;
     if ((dtype == RFSN_BF16 || dtype == RFSN_F16) && head_dim == 128) {
         rfsn_status st = encode_map(&a->maps[0], k_arena, dtype, batch_kv_heads, rows, head_dim, 64);

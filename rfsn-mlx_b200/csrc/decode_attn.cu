@@ -48,7 +48,7 @@ struct Smem {
     int2 tinfo[STAGES];
     float red_m[NCW][SLOTS];
     float red_l[NCW][SLOTS];
-    float red_o[NCW][SLOTS][D];
+    alignas(16) float red_o[NCW][SLOTS][D];
     int flag;
     int abort;
     int call;  // cross-GPU merge: this call's stamp for the group
@@ -360,30 +360,38 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
     }
     named_barrier_sync(1, NCW * 32);
 
-    const int tid = threadIdx.x;  // 0..127
     const int part_base = bh * p.splits * SLOTS;
-    {
-        const int d = tid;
+    if (warp < p.nslots) {
+        // one warp per query slot, lane = output float4: the CTA partial of the slot
+        const int slot = warp;
+        float mw[NCW];
+        float M = -CUDART_INF_F;
+#pragma unroll
+        for (int w = 0; w < NCW; ++w) {
+            mw[w] = sm.red_m[w][slot];
+            M = fmaxf(M, mw[w]);
+        }
+        float L = 0.f;
+        float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (M != -CUDART_INF_F) {
+#pragma unroll
+            for (int w = 0; w < NCW; ++w) {
+                const float wt = exp2f(mw[w] - M);
+                const float4 o = reinterpret_cast<const float4*>(sm.red_o[w][slot])[lane];
+                L += wt * sm.red_l[w][slot];
+                O.x += wt * o.x;
+                O.y += wt * o.y;
+                O.z += wt * o.z;
+                O.w += wt * o.w;
+            }
+        }
         const float inv_ps = 1.f / p.pscale;
-        for (int slot = 0; slot < p.nslots; ++slot) {
-            float M = -CUDART_INF_F;
-#pragma unroll
-            for (int w = 0; w < NCW; ++w) M = fmaxf(M, sm.red_m[w][slot]);
-            float L = 0.f, O = 0.f;
-            if (M != -CUDART_INF_F) {
-#pragma unroll
-                for (int w = 0; w < NCW; ++w) {
-                    const float wt = exp2f(sm.red_m[w][slot] - M);
-                    L += wt * sm.red_l[w][slot];
-                    O += wt * sm.red_o[w][slot][d];
-                }
-            }
-            const int pidx = part_base + split * SLOTS + slot;
-            p.ws.o[(size_t)pidx * D + d] = O * inv_ps;
-            if (d == 0) {
-                p.ws.m[pidx] = M;
-                p.ws.l[pidx] = L;
-            }
+        const int pidx = part_base + split * SLOTS + slot;
+        reinterpret_cast<float4*>(p.ws.o + (size_t)pidx * D)[lane] =
+            make_float4(O.x * inv_ps, O.y * inv_ps, O.z * inv_ps, O.w * inv_ps);
+        if (lane == 0) {
+            p.ws.m[pidx] = M;
+            p.ws.l[pidx] = L;
         }
     }
     // The split merge reuses red_o as scratch once every consumer thread is past
@@ -418,6 +426,12 @@ rfsn_status launch(const CUtensorMap* maps, const Params& p, cudaStream_t stream
 }  // namespace fast
 
 int fast_max_splits() { return fast::MAX_SPLITS; }
+
+void preload_fast_kernels() {
+    cudaFuncAttributes a;
+    cudaFuncGetAttributes(&a, fast::paged_decode_kernel<__nv_bfloat16, 3>);
+    cudaFuncGetAttributes(&a, fast::paged_decode_kernel<__half, 3>);
+}
 
 rfsn_status fast_launch(int dtype, const CUtensorMap* maps, const fast::Params& p, int stages, cudaStream_t stream) {
     if (stages != 3) {

@@ -242,6 +242,16 @@ rfsn_status launch(const Params& p, int groups, cudaStream_t stream) {
 
 }  // namespace generic
 
+void preload_generic_kernels() {
+    cudaFuncAttributes a;
+    cudaFuncGetAttributes(&a, generic::generic_attn_kernel<float, true>);
+    cudaFuncGetAttributes(&a, generic::generic_attn_kernel<float, false>);
+    cudaFuncGetAttributes(&a, generic::generic_attn_kernel<__half, true>);
+    cudaFuncGetAttributes(&a, generic::generic_attn_kernel<__half, false>);
+    cudaFuncGetAttributes(&a, generic::generic_attn_kernel<__nv_bfloat16, true>);
+    cudaFuncGetAttributes(&a, generic::generic_attn_kernel<__nv_bfloat16, false>);
+}
+
 rfsn_status generic_launch(int dtype, bool paged, const generic::Params& p, int groups, cudaStream_t stream) {
     if (p.head_dim > generic::MAX_D) {
         set_error("attention: head_dim %d above %d", p.head_dim, generic::MAX_D);

@@ -38,6 +38,11 @@ __global__ void lse_merge_kernel(const float* __restrict__ parts_out, const floa
 
 }  // namespace
 
+void preload_merge_kernels() {
+    cudaFuncAttributes a;
+    cudaFuncGetAttributes(&a, lse_merge_kernel);
+}
+
 rfsn_status lse_merge_launch(const float* parts_out, const float* parts_lse, int n_parts, int rows, int head_dim,
                              float* out, float* lse_out, cudaStream_t stream) {
     const int threads = head_dim >= 128 ? 128 : ((head_dim + 31) / 32) * 32;

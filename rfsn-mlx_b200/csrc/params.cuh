@@ -99,4 +99,13 @@ rfsn_status rope_append_launch(int dtype, const void* q, const void* k, const vo
 rfsn_status copy_rows_launch(void* ak, void* av, int groups, int rows, int row_bytes, int src_row0, int src_offset,
                              int src_wrap, int dst_row0, int count, cudaStream_t stream);
 
+// Load every kernel of the library on the current device now (under lazy
+// module loading a kernel is otherwise loaded at its first launch, which can
+// stall a decode step by milliseconds, e.g. at the first seal copy).
+void preload_fast_kernels();
+void preload_generic_kernels();
+void preload_ring_kernels();
+void preload_merge_kernels();
+void preload_prefill_kernels();
+
 }  // namespace rfsn

@@ -656,6 +656,12 @@ rfsn_status launch(const CUtensorMap* maps, const PrefillParams& p, cudaStream_t
 
 }  // namespace prefill
 
+void preload_prefill_kernels() {
+    cudaFuncAttributes a;
+    cudaFuncGetAttributes(&a, prefill::prefill_attn_kernel<__nv_bfloat16>);
+    cudaFuncGetAttributes(&a, prefill::prefill_attn_kernel<__half>);
+}
+
 rfsn_status prefill_launch(int dtype, const CUtensorMap* maps, const PrefillParams& p, cudaStream_t stream) {
     if (p.groups_per_kv < 1 || p.groups_per_kv > prefill::BM) {
         set_error("tensor-core prefill: %d query heads per KV head (max %d)", p.groups_per_kv, prefill::BM);

@@ -128,6 +128,14 @@ rfsn_status rope_append_launch(int dtype, const void* q, const void* k, const vo
     return RFSN_OK;
 }
 
+void preload_ring_kernels() {
+    cudaFuncAttributes a;
+    cudaFuncGetAttributes(&a, ring::rope_append_kernel<float, float>);
+    cudaFuncGetAttributes(&a, ring::rope_append_kernel<__half, __half>);
+    cudaFuncGetAttributes(&a, ring::rope_append_kernel<__nv_bfloat16, __nv_bfloat16>);
+    cudaFuncGetAttributes(&a, ring::copy_rows_kernel);
+}
+
 rfsn_status copy_rows_launch(void* ak, void* av, int groups, int rows, int row_bytes, int src_row0, int src_offset,
                              int src_wrap, int dst_row0, int count, cudaStream_t stream) {
     const long total = (long)groups * count * (row_bytes / 16);

@@ -121,6 +121,9 @@ class GraphedDecodeStep:
         self._dptr_k, self._dptr_v = base + n_state + n_q, base + n_state + n_q + n_kv
         self.workspace = native.Workspace(dev)
         self.workspace.get(native.workspace_bytes(B, q_heads, Hkv, 1, D, 0))
+        # rotated q: allocated here, so a capture allocates nothing (a device
+        # allocation inside a capture can cost tens of milliseconds)
+        self.q_rot = torch.empty(self.shape_q, dtype=torch.float32, device=dev)
         self.stream = torch.cuda.Stream(device=dev)
         self.graph: Optional[torch.cuda.CUDAGraph] = None
         self.key = None
@@ -137,7 +140,7 @@ class GraphedDecodeStep:
 
         c = self.cache
         B, H, L, D = self.shape_q
-        q_rot = torch.empty(self.shape_q, dtype=torch.float32, device=c.device)
+        q_rot = self.q_rot
         native.check(
             native.lib().rfsn_rope_append_step(
                 self._dptr_q, self._dptr_k, self._dptr_v, native.dtype_code(c.dtype), c.inv_freq().data_ptr(),

@@ -210,7 +210,7 @@ class GraphedShardedDecodeStep:
 
         c, inner = self.cache, self._inner
         B, H, L, D = inner.shape_q
-        q_rot = torch.empty(inner.shape_q, dtype=torch.float32, device=c.device)
+        q_rot = inner.q_rot
         # the kernels read the pinned staging buffer and write the pinned output across the bus
         native.check(
             native.lib().rfsn_rope_append_step(
