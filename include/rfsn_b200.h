@@ -167,6 +167,23 @@ RFSN_API rfsn_status rfsn_rope_append_step(const void* q, const void* k, const v
                                            int head_dim, float* q_out, const rfsn_arena* arena, int ring_row0,
                                            int capacity, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Dense-layer helpers of the model driver (not on the attention path).
+ *
+ * RMSNorm (layer.py:52-64): out = weight * x / sqrt(mean(x^2) + eps) per row
+ * of n elements, in float32, rounded to dtype once; x, weight and out share
+ * the dtype (RFSN_F32 / F16 / BF16), rows are contiguous. With residual
+ * (and sum_out) non-NULL the row is first s = x + residual rounded to dtype,
+ * written to sum_out, and s is normalised (16-byte aligned rows of at most
+ * 1024 16-byte vectors). */
+RFSN_API rfsn_status rfsn_rms_norm(const void* x, const void* residual, const void* weight, void* sum_out, void* out,
+                                   int rows, int n, int dtype, float eps, void* stream);
+
+/* SwiGLU on a fused gate|up projection (layer.py:164-166): gate_up rows hold
+ * [gate (n), up (n)]; out[r, c] = silu(gate[r, c]) * up[r, c], silu rounded to
+ * dtype first, the product in float32 rounded once. */
+RFSN_API rfsn_status rfsn_silu_mul(const void* gate_up, void* out, int rows, int n, int dtype, void* stream);
+
 /* Launch plan of a tensor-core prefill call of this shape (rfsn_paged_attention
  * with q_len >= 64, bf16/f16 K/V, head_dim 128): the units (query block of
  * 128 / (q_heads / kv_heads) positions x KV head) are launched longest causal

@@ -141,6 +141,7 @@ void preload_kernels_once(int dev) {
     preload_ring_kernels();
     preload_merge_kernels();
     preload_prefill_kernels();
+    preload_model_kernels();
     cudaGetLastError();  // a kernel that cannot be loaded here reports the error at its launch
 }
 
@@ -345,6 +346,22 @@ rfsn_status rfsn_rope_append_step(const void* q, const void* k, const void* v, i
     return rope_append_launch(in_dtype, q, k, v, inv_freq, 0, batch, qh, kv_heads, len, head_dim, q_out, arena->k,
                               arena->v, arena->rows, ring_row0, capacity, 0, static_cast<cudaStream_t>(stream),
                               step_state, step_state_copy);
+}
+
+rfsn_status rfsn_rms_norm(const void* x, const void* residual, const void* weight, void* sum_out, void* out, int rows,
+                          int n, int dtype, float eps, void* stream) {
+    RFSN_CHECK_ARG(x != nullptr && weight != nullptr && out != nullptr, "rfsn_rms_norm: NULL pointer");
+    RFSN_CHECK_ARG((residual == nullptr) == (sum_out == nullptr), "rfsn_rms_norm: residual and sum_out go together");
+    RFSN_CHECK_ARG(rows >= 0 && n > 0 && valid_dtype(dtype), "rfsn_rms_norm: bad shape or dtype");
+    if (rows == 0) return RFSN_OK;
+    return rms_norm_dispatch(dtype, x, residual, weight, sum_out, out, rows, n, eps, static_cast<cudaStream_t>(stream));
+}
+
+rfsn_status rfsn_silu_mul(const void* gate_up, void* out, int rows, int n, int dtype, void* stream) {
+    RFSN_CHECK_ARG(gate_up != nullptr && out != nullptr, "rfsn_silu_mul: NULL pointer");
+    RFSN_CHECK_ARG(rows >= 0 && n > 0 && valid_dtype(dtype), "rfsn_silu_mul: bad shape or dtype");
+    if (rows == 0) return RFSN_OK;
+    return silu_mul_dispatch(dtype, gate_up, out, rows, n, static_cast<cudaStream_t>(stream));
 }
 
 rfsn_status rfsn_prefill_plan(int batch, int q_heads, int kv_heads, int q_len, int q_pos0, int archived_tokens,

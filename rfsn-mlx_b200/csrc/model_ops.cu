@@ -1,0 +1,185 @@
+// Fused dense-layer helpers of the model driver (the reference's layer.py
+// RMSNorm and SwiGLU): one kernel each instead of a chain of elementwise ops.
+#include "params.cuh"
+
+namespace rfsn {
+namespace model_ops {
+
+constexpr int kThreads = 256;
+
+// layer.py:52-64: y = weight * x / sqrt(mean(x^2) + eps) in float32, rounded
+// to the storage type once. One CTA per row.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) rms_norm_kernel(const T* __restrict__ x, const T* __restrict__ w,
+                                                            T* __restrict__ y, int n, float eps) {
+    const T* xr = x + (size_t)blockIdx.x * n;
+    T* yr = y + (size_t)blockIdx.x * n;
+    float s = 0.f;
+    for (int i = threadIdx.x; i < n; i += kThreads) {
+        const float v = to_f32<T>(xr[i]);
+        s += v * v;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    __shared__ float part[kThreads / 32];
+    __shared__ float rms;
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.f;
+        for (int i = 0; i < kThreads / 32; ++i) t += part[i];
+        rms = sqrtf(t / (float)n + eps);
+    }
+    __syncthreads();
+    const float r = rms;
+    for (int i = threadIdx.x; i < n; i += kThreads) {
+        yr[i] = from_f32<T>(to_f32<T>(w[i]) * (to_f32<T>(xr[i]) / r));
+    }
+}
+
+// The same with the row held in registers as 16-byte vectors (all of a
+// thread's loads in flight at once; rows of up to kThreads * PER vectors) and
+// an optional residual added first: s = x + r rounded to T (stored to s_out,
+// the layer's new residual stream), y = weight * s / rms(s).
+template <typename T, int PER>
+__global__ void __launch_bounds__(kThreads) rms_norm_vec_kernel(const T* __restrict__ x, const T* __restrict__ res,
+                                                                const T* __restrict__ w, T* __restrict__ s_out,
+                                                                T* __restrict__ y, int n, float eps) {
+    constexpr int VEC = 16 / sizeof(T);
+    const int nvec = n / VEC;
+    const size_t row = (size_t)blockIdx.x * n;
+    uint4 xv[PER];
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+        const int vi = threadIdx.x + k * kThreads;
+        if (vi < nvec) {
+            xv[k] = *reinterpret_cast<const uint4*>(x + row + (size_t)vi * VEC);
+            if (res != nullptr) {
+                const uint4 rv = *reinterpret_cast<const uint4*>(res + row + (size_t)vi * VEC);
+                T* a = reinterpret_cast<T*>(&xv[k]);
+                const T* b = reinterpret_cast<const T*>(&rv);
+#pragma unroll
+                for (int e = 0; e < VEC; ++e) a[e] = from_f32<T>(to_f32<T>(a[e]) + to_f32<T>(b[e]));
+                *reinterpret_cast<uint4*>(s_out + row + (size_t)vi * VEC) = xv[k];
+            }
+            const T* a = reinterpret_cast<const T*>(&xv[k]);
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) {
+                const float v = to_f32<T>(a[e]);
+                s += v * v;
+            }
+        }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    __shared__ float part[kThreads / 32];
+    __shared__ float rms;
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.f;
+        for (int i = 0; i < kThreads / 32; ++i) t += part[i];
+        rms = sqrtf(t / (float)n + eps);
+    }
+    __syncthreads();
+    const float r = rms;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+        const int vi = threadIdx.x + k * kThreads;
+        if (vi < nvec) {
+            const uint4 wv = *reinterpret_cast<const uint4*>(w + (size_t)vi * VEC);
+            const T* a = reinterpret_cast<const T*>(&xv[k]);
+            const T* b = reinterpret_cast<const T*>(&wv);
+            uint4 ov;
+            T* o = reinterpret_cast<T*>(&ov);
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) o[e] = from_f32<T>(to_f32<T>(b[e]) * (to_f32<T>(a[e]) / r));
+            *reinterpret_cast<uint4*>(y + row + (size_t)vi * VEC) = ov;
+        }
+    }
+}
+
+// layer.py:164-166 SwiGLU on a fused gate|up projection row [2n]: y = silu(g) * u,
+// silu rounded to the storage type first (as an elementwise op would), the
+// product in float32 rounded once.
+template <typename T>
+__global__ void silu_mul_kernel(const T* __restrict__ gu, T* __restrict__ y, long long rows, int n) {
+    const long long total = rows * n;
+    for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+         idx += (long long)gridDim.x * blockDim.x) {
+        const long long r = idx / n;
+        const int c = (int)(idx - r * n);
+        const float g = to_f32<T>(gu[r * 2 * n + c]);
+        const float u = to_f32<T>(gu[r * 2 * n + n + c]);
+        const float s = to_f32<T>(from_f32<T>(g / (1.f + expf(-g))));
+        y[idx] = from_f32<T>(s * u);
+    }
+}
+
+constexpr int kVecPer = 4;  // vectors per thread held in registers: rows up to 8192 bf16 / 4096 fp32 elements
+
+template <typename T>
+rfsn_status rms_norm_launch(const void* x, const void* res, const void* w, void* s_out, void* y, int rows, int n,
+                            float eps, cudaStream_t s) {
+    constexpr int VEC = 16 / sizeof(T);
+    const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(res) |
+                           reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(s_out) |
+                           reinterpret_cast<uintptr_t>(y)) & 15) == 0;
+    if (aligned && n % VEC == 0 && n / VEC <= kThreads * kVecPer) {
+        rms_norm_vec_kernel<T, kVecPer><<<rows, kThreads, 0, s>>>(
+            static_cast<const T*>(x), static_cast<const T*>(res), static_cast<const T*>(w), static_cast<T*>(s_out),
+            static_cast<T*>(y), n, eps);
+    } else {
+        if (res != nullptr) {
+            set_error("rfsn_rms_norm: a residual needs 16-byte aligned rows of at most %d vectors", kThreads * kVecPer);
+            return RFSN_ERR_UNSUPPORTED;
+        }
+        rms_norm_kernel<T><<<rows, kThreads, 0, s>>>(static_cast<const T*>(x), static_cast<const T*>(w),
+                                                     static_cast<T*>(y), n, eps);
+    }
+    RFSN_CUDA(cudaGetLastError());
+    note_launch();
+    return RFSN_OK;
+}
+
+template <typename T>
+rfsn_status silu_mul_launch(const void* gu, void* y, int rows, int n, cudaStream_t s) {
+    const long long total = (long long)rows * n;
+    long long blocks = (total + kThreads - 1) / kThreads;
+    if (blocks > 148LL * 16) blocks = 148LL * 16;
+    silu_mul_kernel<T><<<(unsigned)blocks, kThreads, 0, s>>>(static_cast<const T*>(gu), static_cast<T*>(y), rows, n);
+    RFSN_CUDA(cudaGetLastError());
+    note_launch();
+    return RFSN_OK;
+}
+
+}  // namespace model_ops
+
+void preload_model_kernels() {
+    cudaFuncAttributes a;
+    cudaFuncGetAttributes(&a, model_ops::rms_norm_kernel<float>);
+    cudaFuncGetAttributes(&a, model_ops::rms_norm_kernel<__half>);
+    cudaFuncGetAttributes(&a, model_ops::rms_norm_kernel<__nv_bfloat16>);
+    cudaFuncGetAttributes(&a, model_ops::rms_norm_vec_kernel<float, model_ops::kVecPer>);
+    cudaFuncGetAttributes(&a, model_ops::rms_norm_vec_kernel<__half, model_ops::kVecPer>);
+    cudaFuncGetAttributes(&a, model_ops::rms_norm_vec_kernel<__nv_bfloat16, model_ops::kVecPer>);
+    cudaFuncGetAttributes(&a, model_ops::silu_mul_kernel<float>);
+    cudaFuncGetAttributes(&a, model_ops::silu_mul_kernel<__half>);
+    cudaFuncGetAttributes(&a, model_ops::silu_mul_kernel<__nv_bfloat16>);
+}
+
+rfsn_status rms_norm_dispatch(int dtype, const void* x, const void* res, const void* w, void* s_out, void* y, int rows,
+                              int n, float eps, cudaStream_t s) {
+    if (dtype == RFSN_F32) return model_ops::rms_norm_launch<float>(x, res, w, s_out, y, rows, n, eps, s);
+    if (dtype == RFSN_F16) return model_ops::rms_norm_launch<__half>(x, res, w, s_out, y, rows, n, eps, s);
+    return model_ops::rms_norm_launch<__nv_bfloat16>(x, res, w, s_out, y, rows, n, eps, s);
+}
+
+rfsn_status silu_mul_dispatch(int dtype, const void* gu, void* y, int rows, int n, cudaStream_t s) {
+    if (dtype == RFSN_F32) return model_ops::silu_mul_launch<float>(gu, y, rows, n, s);
+    if (dtype == RFSN_F16) return model_ops::silu_mul_launch<__half>(gu, y, rows, n, s);
+    return model_ops::silu_mul_launch<__nv_bfloat16>(gu, y, rows, n, s);
+}
+
+}  // namespace rfsn

@@ -107,5 +107,10 @@ void preload_generic_kernels();
 void preload_ring_kernels();
 void preload_merge_kernels();
 void preload_prefill_kernels();
+void preload_model_kernels();
+
+rfsn_status rms_norm_dispatch(int dtype, const void* x, const void* res, const void* w, void* s_out, void* y, int rows,
+                              int n, float eps, cudaStream_t s);
+rfsn_status silu_mul_dispatch(int dtype, const void* gu, void* y, int rows, int n, cudaStream_t s);
 
 }  // namespace rfsn

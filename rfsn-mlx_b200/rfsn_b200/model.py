@@ -36,11 +36,48 @@ from .layer import attention_step, capture_graph
 ArrayLike = Union[np.ndarray, torch.Tensor]
 
 
+def _dense_device_check(x: torch.Tensor) -> None:
+    if not x.is_cuda:
+        raise native.NativeUnavailable("the model's layers run on a CUDA device (no CPU path)")
+
+
 def _rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
-    """layer.py:52-64: weight * x / sqrt(mean(x^2) + eps), computed in float32."""
-    xf = x.float()
-    rms = torch.sqrt(torch.mean(xf * xf, dim=-1, keepdim=True) + eps)
-    return (weight.float() * (xf / rms)).to(x.dtype)
+    """layer.py:52-64: weight * x / sqrt(mean(x^2) + eps), computed in float32
+    and rounded once (one fused kernel, ``rfsn_rms_norm``)."""
+    _dense_device_check(x)
+    xc = x.contiguous()
+    out = torch.empty_like(xc)
+    n = int(xc.shape[-1])
+    native.check(native.lib().rfsn_rms_norm(xc.data_ptr(), None, weight.data_ptr(), None, out.data_ptr(),
+                                            xc.numel() // n, n, native.dtype_code(xc.dtype), float(eps),
+                                            native.stream_ptr()), "rfsn_rms_norm")
+    return out
+
+
+def _add_rms_norm(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor,
+                  eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+    """(s, norm(s)) with s = residual + x in the storage type (the layer's
+    residual add and the following RMSNorm as one kernel)."""
+    _dense_device_check(x)
+    xc, rc = x.contiguous(), residual.contiguous()
+    s, out = torch.empty_like(xc), torch.empty_like(xc)
+    n = int(xc.shape[-1])
+    native.check(native.lib().rfsn_rms_norm(xc.data_ptr(), rc.data_ptr(), weight.data_ptr(), s.data_ptr(),
+                                            out.data_ptr(), xc.numel() // n, n, native.dtype_code(xc.dtype),
+                                            float(eps), native.stream_ptr()), "rfsn_rms_norm")
+    return s, out
+
+
+def _silu_mul(gate_up: torch.Tensor) -> torch.Tensor:
+    """layer.py:164-166 on a fused gate|up projection [..., 2F]: silu(gate) * up
+    (one kernel, ``rfsn_silu_mul``)."""
+    _dense_device_check(gate_up)
+    gu = gate_up.contiguous()
+    n = int(gu.shape[-1]) // 2
+    out = torch.empty(tuple(gu.shape[:-1]) + (n,), dtype=gu.dtype, device=gu.device)
+    native.check(native.lib().rfsn_silu_mul(gu.data_ptr(), out.data_ptr(), gu.numel() // (2 * n), n,
+                                            native.dtype_code(gu.dtype), native.stream_ptr()), "rfsn_silu_mul")
+    return out
 
 
 def _layer_norm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float) -> torch.Tensor:
@@ -51,10 +88,15 @@ def _layer_norm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: 
 class RFSNLayer:
     """One transformer layer (layer.py:67-167) with the attention step on the CUDA path."""
 
-    def __init__(self, config: RFSNConfig, layer_idx: int, params: Dict[str, torch.Tensor]) -> None:
+    def __init__(self, config: RFSNConfig, layer_idx: int, params: Dict[str, torch.Tensor],
+                 w_qkv: torch.Tensor, w_gate_up: torch.Tensor) -> None:
         self.config = config
         self.layer_idx = layer_idx
-        self.p = params  # views into the model's parameter dict for this layer
+        self.p = params  # the model's parameter dict
+        # q|k|v and gate|up projections stored as one matrix each (the named
+        # parameters are views of their rows): one GEMV instead of three / two
+        self.w_qkv = w_qkv
+        self.w_gate_up = w_gate_up
 
     def _w(self, name: str) -> torch.Tensor:
         return self.p[f"layers.{self.layer_idx}.{name}"]
@@ -66,15 +108,15 @@ class RFSNLayer:
         H, Hkv, D = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
         residual = x
         xn = _rms_norm(x, self._w("attn_norm.weight"), cfg.norm_eps)
-        q = F.linear(xn, self._w("q_proj.weight")).reshape(B, L, H, D).transpose(1, 2)
-        k = F.linear(xn, self._w("k_proj.weight")).reshape(B, L, Hkv, D).transpose(1, 2)
-        v = F.linear(xn, self._w("v_proj.weight")).reshape(B, L, Hkv, D).transpose(1, 2)
+        qkv = F.linear(xn, self.w_qkv)
+        q = qkv[..., :H * D].reshape(B, L, H, D).transpose(1, 2)
+        k = qkv[..., H * D:(H + Hkv) * D].reshape(B, L, Hkv, D).transpose(1, 2)
+        v = qkv[..., (H + Hkv) * D:].reshape(B, L, Hkv, D).transpose(1, 2)
         a = attention_step(q, k, v, layer_cache, start_pos) if attn is None else attn(q, k, v)  # float32 [B, H, L, D]
         attn = a.transpose(1, 2).reshape(B, L, H * D).to(x.dtype)
-        x = residual + F.linear(attn, self._w("o_proj.weight"))
-        h = _rms_norm(x, self._w("ffn_norm.weight"), cfg.norm_eps)
-        ffn = F.linear(F.silu(F.linear(h, self._w("gate_proj.weight"))) * F.linear(h, self._w("up_proj.weight")),
-                       self._w("down_proj.weight"))
+        x, h = _add_rms_norm(F.linear(attn, self._w("o_proj.weight")), residual, self._w("ffn_norm.weight"),
+                             cfg.norm_eps)
+        ffn = F.linear(_silu_mul(F.linear(h, self.w_gate_up)), self._w("down_proj.weight"))
         return x + ffn
 
 
@@ -91,6 +133,18 @@ class RFSNModel:
         # model initialises in seconds); norms start at ones / zeros
         gen = torch.Generator(device=self.device)
         gen.manual_seed(0 if seed is None else seed)
+        Hd, H, Hkv, D, Fd = config.hidden_dim, config.num_heads, config.num_kv_heads, config.head_dim, config.ffn_dim
+        fused = []
+        for i in range(config.num_layers):  # the fused matrices own the q/k/v and gate/up rows
+            pre = f"layers.{i}."
+            w_qkv = torch.empty(((H + 2 * Hkv) * D, Hd), device=self.device, dtype=self.dtype)
+            w_gu = torch.empty((2 * Fd, Hd), device=self.device, dtype=self.dtype)
+            self.params[pre + "q_proj.weight"] = w_qkv[:H * D]
+            self.params[pre + "k_proj.weight"] = w_qkv[H * D:(H + Hkv) * D]
+            self.params[pre + "v_proj.weight"] = w_qkv[(H + Hkv) * D:]
+            self.params[pre + "gate_proj.weight"] = w_gu[:Fd]
+            self.params[pre + "up_proj.weight"] = w_gu[Fd:]
+            fused.append((w_qkv, w_gu))
         for name, shape in self.parameter_shapes().items():
             if name.endswith("norm.weight"):
                 t = torch.ones(shape, device=self.device, dtype=self.dtype)
@@ -99,8 +153,11 @@ class RFSNModel:
             else:
                 t = torch.empty(shape, device=self.device, dtype=torch.float32).normal_(0.0, 0.02, generator=gen)
                 t = t.to(self.dtype)
-            self.params[name] = t
-        self.layers = [RFSNLayer(config, i, self.params) for i in range(config.num_layers)]
+            if name in self.params:
+                self.params[name].copy_(t)
+            else:
+                self.params[name] = t
+        self.layers = [RFSNLayer(config, i, self.params, *fused[i]) for i in range(config.num_layers)]
         self.use_graphs = True
         self._graph: Optional["_DecodeGraph"] = None
 

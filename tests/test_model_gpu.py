@@ -9,6 +9,7 @@ blocks, so the segmented path is exercised."""
 import numpy as np
 import pytest
 import torch
+import torch.nn.functional as F
 
 from _util import GOLDEN
 from test_model_cpu import tiny_config
@@ -267,3 +268,33 @@ def test_decode_graph_falls_back_when_blocks_are_cold(tmp_path):
         assert torch.equal(oe, og)
         tok = torch.argmax(oe, dim=-1).to(torch.int32)
     assert c_g.layer(0).residency_manager.get_metrics() == c_e.layer(0).residency_manager.get_metrics()
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_fused_rms_norm_and_swiglu_match_the_elementwise_formulas(dtype):
+    """rfsn_rms_norm / rfsn_silu_mul against the reference's elementwise
+    formulas (layer.py:52-64, :164-166) evaluated in torch: equal up to one
+    rounding of the storage type (different summation order of the mean)."""
+    from rfsn_b200.model import _add_rms_norm, _rms_norm, _silu_mul
+
+    gen = torch.Generator(device="cuda").manual_seed(11)
+    for rows, n in ((1, 4096), (7, 128), (3, 1000)):
+        x = (torch.randn((rows, n), generator=gen, device="cuda") * 3).to(dtype)
+        w = (torch.rand((n,), generator=gen, device="cuda") + 0.5).to(dtype)
+        xf = x.float()
+        want = (w.float() * (xf / torch.sqrt(torch.mean(xf * xf, dim=-1, keepdim=True) + 1e-5))).to(dtype)
+        got = _rms_norm(x, w, 1e-5)
+        ulp = {torch.float32: 2e-6, torch.bfloat16: 8e-3, torch.float16: 1e-3}[dtype]
+        assert torch.allclose(got.float(), want.float(), rtol=ulp, atol=ulp), (rows, n)
+        if n % 8 == 0:  # residual add fused in (16-byte rows)
+            r = torch.randn((rows, n), generator=gen, device="cuda").to(dtype)
+            s_want = r + x
+            sf = s_want.float()
+            want = (w.float() * (sf / torch.sqrt(torch.mean(sf * sf, dim=-1, keepdim=True) + 1e-5))).to(dtype)
+            s_got, got = _add_rms_norm(x, r, w, 1e-5)
+            assert torch.equal(s_got, s_want), (rows, n)
+            assert torch.allclose(got.float(), want.float(), rtol=ulp, atol=ulp), (rows, n)
+        gu = (torch.randn((rows, 2 * n), generator=gen, device="cuda") * 4).to(dtype)
+        want = F.silu(gu[:, :n]) * gu[:, n:]
+        got = _silu_mul(gu)
+        assert torch.allclose(got.float(), want.float(), rtol=ulp, atol=ulp), (rows, n)
