@@ -20,8 +20,9 @@ scaling: the context is fixed.
 
 Reported (rank 0, one JSON line): device throughput with inputs resident in
 HBM (CUDA-graph-captured calls timed with CUDA events, max over ranks),
-``e2e`` through the public API with the new token's q/k/v copied from pinned
-host memory and the output read back every call, the decode kernel's
+``e2e`` through the public API with the new token's q/k/v taken from pinned
+host memory and the output returned to pinned host memory every call (the
+kernels read and write those buffers across the bus), the decode kernel's
 roofline against the measured HBM copy bandwidth, NVML clock samples taken
 during the timed region, and (N = 1) a CPU baseline: the reference algorithm
 restated in numpy, on the host's cores. ``--impl reference`` prints that CPU
