@@ -839,9 +839,9 @@ def run_model(args):
         "decode_ms_per_token": dec_ms / (n_decode - 1),
         "prefill_tokens_per_s": 4096 / (pre_ms / 1e3), "prefill_ms": pre_ms,
         "archived_blocks_after": blocks,
-        "notes": "projections and the LM head are cuBLAS GEMMs (q|k|v and gate|up fused); RMSNorm (+ residual add), "
-                 "SwiGLU and attention (RoPE+append, seal, paged attention, tcgen05 prefill) run on this library's "
-                 "kernels",
+        "notes": "q|k|v and gate|up fused; decode projections on this library's GEMV, prefill projections and the "
+                 "LM head on cuBLAS; RMSNorm (+ residual add), SwiGLU and attention (RoPE+append, seal, paged "
+                 "attention, tcgen05 prefill) on this library's kernels",
     }
     print(json.dumps(line), flush=True)
     return 0

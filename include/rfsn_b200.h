@@ -184,6 +184,12 @@ RFSN_API rfsn_status rfsn_rms_norm(const void* x, const void* residual, const vo
  * dtype first, the product in float32 rounded once. */
 RFSN_API rfsn_status rfsn_silu_mul(const void* gate_up, void* out, int rows, int n, int dtype, void* stream);
 
+/* y[r, n] = sum_k weight[n, k] * x[r, k] for rows = 1..4 rows of x (a decode
+ * token's projection; weight [n_out, k] row-major, 16-byte aligned rows),
+ * float32 accumulation, y [rows, n_out] rounded to dtype once. */
+RFSN_API rfsn_status rfsn_gemv(const void* weight, const void* x, void* y, int n_out, int k, int rows, int dtype,
+                               void* stream);
+
 /* Launch plan of a tensor-core prefill call of this shape (rfsn_paged_attention
  * with q_len >= 64, bf16/f16 K/V, head_dim 128): the units (query block of
  * 128 / (q_heads / kv_heads) positions x KV head) are launched longest causal

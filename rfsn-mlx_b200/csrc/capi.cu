@@ -364,6 +364,17 @@ rfsn_status rfsn_silu_mul(const void* gate_up, void* out, int rows, int n, int d
     return silu_mul_dispatch(dtype, gate_up, out, rows, n, static_cast<cudaStream_t>(stream));
 }
 
+rfsn_status rfsn_gemv(const void* weight, const void* x, void* y, int n_out, int k, int rows, int dtype, void* stream) {
+    RFSN_CHECK_ARG(weight != nullptr && x != nullptr && y != nullptr, "rfsn_gemv: NULL pointer");
+    RFSN_CHECK_ARG(valid_dtype(dtype) && n_out > 0 && k > 0 && rows >= 1 && rows <= gemv_max_rows(),
+                   "rfsn_gemv: bad shape or dtype (rows of x: 1..%d)", gemv_max_rows());
+    const int vec = 16 / dtype_size(dtype);
+    RFSN_CHECK_ARG(k % vec == 0 && reinterpret_cast<uintptr_t>(weight) % 16 == 0,
+                   "rfsn_gemv: weight rows must be 16-byte aligned (k a multiple of %d)", vec);
+    RFSN_CHECK_ARG((size_t)rows * k * sizeof(float) <= 200 * 1024, "rfsn_gemv: x too large for shared memory");
+    return gemv_dispatch(dtype, weight, x, y, n_out, k, rows, static_cast<cudaStream_t>(stream));
+}
+
 rfsn_status rfsn_prefill_plan(int batch, int q_heads, int kv_heads, int q_len, int q_pos0, int archived_tokens,
                               int hot_start, int hot_length, int* cta_units_whole, int* tail_splits, int* ctas) {
     RFSN_CHECK_ARG(cta_units_whole != nullptr && tail_splits != nullptr && ctas != nullptr, "rfsn_prefill_plan: NULL output");

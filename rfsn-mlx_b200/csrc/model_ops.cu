@@ -117,6 +117,82 @@ __global__ void silu_mul_kernel(const T* __restrict__ gu, T* __restrict__ y, lon
     }
 }
 
+// y[r, n] = sum_k W[n, k] * x[r, k] for a few rows r of x (decode: one token):
+// W [N, K] row-major in the storage type, read once with 16-byte loads, x
+// staged in shared memory (float32), float32 accumulation, y rounded once.
+// Each warp owns ROWS consecutive output columns n at a time (their loads in
+// flight together); lanes stride K in 16-byte vectors.
+constexpr int GV_THREADS = 256;
+constexpr int GV_MAX_X = 4;  // rows of x handled per launch
+
+template <typename T, int XR, int ROWS>
+__global__ void __launch_bounds__(GV_THREADS, XR == 1 ? 2 : 1) gemv_kernel(const T* __restrict__ w,
+                                                                           const T* __restrict__ x,
+                                                                           T* __restrict__ y, int N, int K, int xrows) {
+    extern __shared__ float4 xs4[];  // [xrows][K / 4]
+    float* xs = reinterpret_cast<float*>(xs4);
+    for (int i = threadIdx.x; i < xrows * K; i += GV_THREADS) xs[i] = to_f32<T>(x[i]);
+    __syncthreads();
+    constexpr int VEC = 16 / sizeof(T);  // elements per 16-byte load
+    constexpr int U = (16 + ROWS - 1) / ROWS;  // K steps whose loads are issued together (~16 per lane)
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nvec = K / VEC;
+    const int warps_total = gridDim.x * (GV_THREADS / 32);
+    for (int n0 = (blockIdx.x * (GV_THREADS / 32) + warp) * ROWS; n0 < N; n0 += warps_total * ROWS) {
+        float acc[ROWS][XR];
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r)
+#pragma unroll
+            for (int j = 0; j < XR; ++j) acc[r][j] = 0.f;
+        for (int v0 = lane; v0 < nvec; v0 += 32 * U) {
+            uint4 wv[U][ROWS];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int v = v0 + 32 * u;
+#pragma unroll
+                for (int r = 0; r < ROWS; ++r) {
+                    wv[u][r] = (v < nvec && n0 + r < N)
+                                   ? __ldcs(reinterpret_cast<const uint4*>(w + (size_t)(n0 + r) * K) + v)
+                                   : make_uint4(0, 0, 0, 0);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int v = v0 + 32 * u;
+                if (v >= nvec) break;
+#pragma unroll
+                for (int j = 0; j < XR; ++j) {
+                    if (j >= xrows) break;
+                    float xv[VEC];
+#pragma unroll
+                    for (int q4 = 0; q4 < VEC / 4; ++q4) {
+                        const float4 t = xs4[(j * K + v * VEC) / 4 + q4];
+                        xv[4 * q4] = t.x;
+                        xv[4 * q4 + 1] = t.y;
+                        xv[4 * q4 + 2] = t.z;
+                        xv[4 * q4 + 3] = t.w;
+                    }
+#pragma unroll
+                    for (int r = 0; r < ROWS; ++r) {
+                        const T* e = reinterpret_cast<const T*>(&wv[u][r]);
+#pragma unroll
+                        for (int q = 0; q < VEC; ++q) acc[r][j] += to_f32<T>(e[q]) * xv[q];
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r)
+#pragma unroll
+            for (int j = 0; j < XR; ++j) {
+                float a = acc[r][j];
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
+                if (lane == 0 && j < xrows && n0 + r < N) y[(size_t)j * N + n0 + r] = from_f32<T>(a);
+            }
+    }
+}
+
 constexpr int kVecPer = 4;  // vectors per thread held in registers: rows up to 8192 bf16 / 4096 fp32 elements
 
 template <typename T>
@@ -143,6 +219,44 @@ rfsn_status rms_norm_launch(const void* x, const void* res, const void* w, void*
     return RFSN_OK;
 }
 
+template <typename T, int XR, int ROWS>
+rfsn_status gemv_launch_rows(const void* w, const void* x, void* y, int N, int K, int xrows, int blocks,
+                             cudaStream_t s) {
+    const size_t smem = sizeof(float) * (size_t)xrows * K;
+    auto kern = gemv_kernel<T, XR, ROWS>;
+    RFSN_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    kern<<<blocks, GV_THREADS, smem, s>>>(static_cast<const T*>(w), static_cast<const T*>(x), static_cast<T*>(y), N, K,
+                                          xrows);
+    RFSN_CUDA(cudaGetLastError());
+    note_launch();
+    return RFSN_OK;
+}
+
+// Rows per warp: the count (2, 3 or 4) that fills the most of two CTAs per SM
+// in one pass (4 with a loop when N is larger).
+template <typename T, int XR>
+rfsn_status gemv_launch_xr(const void* w, const void* x, void* y, int N, int K, int xrows, cudaStream_t s) {
+    const int slots = 148 * (XR == 1 ? 2 : 1), warps_per_cta = GV_THREADS / 32;  // resident CTAs
+    int best_rows = 4, best_ctas = 0;
+    for (int rows = 4; rows >= 2; --rows) {
+        const int ctas = (N + rows * warps_per_cta - 1) / (rows * warps_per_cta);
+        if (ctas <= slots && ctas > best_ctas) {
+            best_ctas = ctas;
+            best_rows = rows;
+        }
+    }
+    if (best_ctas == 0) best_ctas = slots;  // more rows than one pass: warps loop
+    if (best_rows == 2) return gemv_launch_rows<T, XR, 2>(w, x, y, N, K, xrows, best_ctas, s);
+    if (best_rows == 3) return gemv_launch_rows<T, XR, 3>(w, x, y, N, K, xrows, best_ctas, s);
+    return gemv_launch_rows<T, XR, 4>(w, x, y, N, K, xrows, best_ctas, s);
+}
+
+template <typename T>
+rfsn_status gemv_launch(const void* w, const void* x, void* y, int N, int K, int xrows, cudaStream_t s) {
+    return xrows == 1 ? gemv_launch_xr<T, 1>(w, x, y, N, K, xrows, s)
+                      : gemv_launch_xr<T, GV_MAX_X>(w, x, y, N, K, xrows, s);
+}
+
 template <typename T>
 rfsn_status silu_mul_launch(const void* gu, void* y, int rows, int n, cudaStream_t s) {
     const long long total = (long long)rows * n;
@@ -156,6 +270,17 @@ rfsn_status silu_mul_launch(const void* gu, void* y, int rows, int n, cudaStream
 
 }  // namespace model_ops
 
+template <typename T>
+void preload_gemv() {
+    cudaFuncAttributes a;
+    cudaFuncGetAttributes(&a, model_ops::gemv_kernel<T, 1, 2>);
+    cudaFuncGetAttributes(&a, model_ops::gemv_kernel<T, 1, 3>);
+    cudaFuncGetAttributes(&a, model_ops::gemv_kernel<T, 1, 4>);
+    cudaFuncGetAttributes(&a, model_ops::gemv_kernel<T, model_ops::GV_MAX_X, 2>);
+    cudaFuncGetAttributes(&a, model_ops::gemv_kernel<T, model_ops::GV_MAX_X, 3>);
+    cudaFuncGetAttributes(&a, model_ops::gemv_kernel<T, model_ops::GV_MAX_X, 4>);
+}
+
 void preload_model_kernels() {
     cudaFuncAttributes a;
     cudaFuncGetAttributes(&a, model_ops::rms_norm_kernel<float>);
@@ -164,6 +289,9 @@ void preload_model_kernels() {
     cudaFuncGetAttributes(&a, model_ops::rms_norm_vec_kernel<float, model_ops::kVecPer>);
     cudaFuncGetAttributes(&a, model_ops::rms_norm_vec_kernel<__half, model_ops::kVecPer>);
     cudaFuncGetAttributes(&a, model_ops::rms_norm_vec_kernel<__nv_bfloat16, model_ops::kVecPer>);
+    preload_gemv<float>();
+    preload_gemv<__half>();
+    preload_gemv<__nv_bfloat16>();
     cudaFuncGetAttributes(&a, model_ops::silu_mul_kernel<float>);
     cudaFuncGetAttributes(&a, model_ops::silu_mul_kernel<__half>);
     cudaFuncGetAttributes(&a, model_ops::silu_mul_kernel<__nv_bfloat16>);
@@ -181,5 +309,13 @@ rfsn_status silu_mul_dispatch(int dtype, const void* gu, void* y, int rows, int 
     if (dtype == RFSN_F16) return model_ops::silu_mul_launch<__half>(gu, y, rows, n, s);
     return model_ops::silu_mul_launch<__nv_bfloat16>(gu, y, rows, n, s);
 }
+
+rfsn_status gemv_dispatch(int dtype, const void* w, const void* x, void* y, int N, int K, int xrows, cudaStream_t s) {
+    if (dtype == RFSN_F32) return model_ops::gemv_launch<float>(w, x, y, N, K, xrows, s);
+    if (dtype == RFSN_F16) return model_ops::gemv_launch<__half>(w, x, y, N, K, xrows, s);
+    return model_ops::gemv_launch<__nv_bfloat16>(w, x, y, N, K, xrows, s);
+}
+
+int gemv_max_rows() { return model_ops::GV_MAX_X; }
 
 }  // namespace rfsn

@@ -112,5 +112,7 @@ void preload_model_kernels();
 rfsn_status rms_norm_dispatch(int dtype, const void* x, const void* res, const void* w, void* s_out, void* y, int rows,
                               int n, float eps, cudaStream_t s);
 rfsn_status silu_mul_dispatch(int dtype, const void* gu, void* y, int rows, int n, cudaStream_t s);
+rfsn_status gemv_dispatch(int dtype, const void* w, const void* x, void* y, int N, int K, int xrows, cudaStream_t s);
+int gemv_max_rows();
 
 }  // namespace rfsn

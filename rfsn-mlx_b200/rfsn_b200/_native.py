@@ -68,6 +68,7 @@ EXPORTED_SYMBOLS = (
     "rfsn_prefill_plan",
     "rfsn_rms_norm",
     "rfsn_silu_mul",
+    "rfsn_gemv",
 )
 
 
@@ -149,6 +150,7 @@ def load_library() -> ctypes.CDLL:
         "rfsn_prefill_plan": (i32, [i32] * 8 + [ctypes.POINTER(ctypes.c_int)] * 3),
         "rfsn_rms_norm": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, ctypes.c_float, vp]),
         "rfsn_silu_mul": (i32, [vp, vp, i32, i32, i32, vp]),
+        "rfsn_gemv": (i32, [vp, vp, vp, i32, i32, i32, i32, vp]),
         "rfsn_arena_copy_rows": (i32, [vp, i32, i32, i32, i32, i32, vp]),
         "rfsn_block_upload": (i32, [vp, i32, i32, vp, vp, vp, vp]),
         "rfsn_block_download": (i32, [vp, i32, i32, vp, vp, vp, vp]),

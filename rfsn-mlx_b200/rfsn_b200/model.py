@@ -68,6 +68,26 @@ def _add_rms_norm(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor,
     return s, out
 
 
+_GEMV_MAX_ROWS = 4
+
+
+def _linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """x @ w^T. Decode-sized inputs (<= 4 rows, 16-byte weight rows) run on this
+    library's GEMV (``rfsn_gemv``: weights streamed once with 16-byte loads,
+    float32 accumulation); larger ones on cuBLAS (``F.linear``)."""
+    K = int(x.shape[-1])
+    rows = x.numel() // K
+    vec = 16 // x.element_size()
+    if (x.is_cuda and rows <= _GEMV_MAX_ROWS and x.dtype == w.dtype and w.is_contiguous() and K % vec == 0
+            and w.data_ptr() % 16 == 0 and rows * K * 4 <= 200 * 1024):
+        xc = x.contiguous()
+        y = torch.empty(tuple(x.shape[:-1]) + (int(w.shape[0]),), dtype=x.dtype, device=x.device)
+        native.check(native.lib().rfsn_gemv(w.data_ptr(), xc.data_ptr(), y.data_ptr(), int(w.shape[0]), K, rows,
+                                            native.dtype_code(x.dtype), native.stream_ptr()), "rfsn_gemv")
+        return y
+    return F.linear(x, w)
+
+
 def _silu_mul(gate_up: torch.Tensor) -> torch.Tensor:
     """layer.py:164-166 on a fused gate|up projection [..., 2F]: silu(gate) * up
     (one kernel, ``rfsn_silu_mul``)."""
@@ -108,15 +128,15 @@ class RFSNLayer:
         H, Hkv, D = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
         residual = x
         xn = _rms_norm(x, self._w("attn_norm.weight"), cfg.norm_eps)
-        qkv = F.linear(xn, self.w_qkv)
+        qkv = _linear(xn, self.w_qkv)
         q = qkv[..., :H * D].reshape(B, L, H, D).transpose(1, 2)
         k = qkv[..., H * D:(H + Hkv) * D].reshape(B, L, Hkv, D).transpose(1, 2)
         v = qkv[..., (H + Hkv) * D:].reshape(B, L, Hkv, D).transpose(1, 2)
         a = attention_step(q, k, v, layer_cache, start_pos) if attn is None else attn(q, k, v)  # float32 [B, H, L, D]
         attn = a.transpose(1, 2).reshape(B, L, H * D).to(x.dtype)
-        x, h = _add_rms_norm(F.linear(attn, self._w("o_proj.weight")), residual, self._w("ffn_norm.weight"),
+        x, h = _add_rms_norm(_linear(attn, self._w("o_proj.weight")), residual, self._w("ffn_norm.weight"),
                              cfg.norm_eps)
-        ffn = F.linear(_silu_mul(F.linear(h, self.w_gate_up)), self._w("down_proj.weight"))
+        ffn = _linear(_silu_mul(_linear(h, self.w_gate_up)), self._w("down_proj.weight"))
         return x + ffn
 
 

@@ -298,3 +298,19 @@ def test_fused_rms_norm_and_swiglu_match_the_elementwise_formulas(dtype):
         want = F.silu(gu[:, :n]) * gu[:, n:]
         got = _silu_mul(gu)
         assert torch.allclose(got.float(), want.float(), rtol=ulp, atol=ulp), (rows, n)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("rows,n,k", [(1, 4096, 4096), (1, 6144, 4096), (1, 1000, 14336), (3, 257, 512), (4, 96, 128)])
+def test_decode_gemv_matches_float32_product(dtype, rows, n, k):
+    """rfsn_gemv (the model's decode projections) against the float32 product
+    rounded once: within one rounding of the storage type."""
+    from rfsn_b200.model import _linear
+
+    gen = torch.Generator(device="cuda").manual_seed(rows * 7 + n)
+    w = (torch.randn((n, k), generator=gen, device="cuda") * 0.05).to(dtype)
+    x = torch.randn((rows, k), generator=gen, device="cuda").to(dtype)
+    want = (x.double() @ w.double().T).float()
+    got = _linear(x, w).float()
+    tol = {torch.float32: 1e-4, torch.bfloat16: 1.6e-2, torch.float16: 2e-3}[dtype]
+    assert torch.allclose(got, want, rtol=tol, atol=tol * float(want.abs().max())), float((got - want).abs().max())
