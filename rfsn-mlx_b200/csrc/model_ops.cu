@@ -12,6 +12,8 @@ constexpr int kThreads = 256;
 template <typename T>
 __global__ void __launch_bounds__(kThreads) rms_norm_kernel(const T* __restrict__ x, const T* __restrict__ w,
                                                             T* __restrict__ y, int n, float eps) {
+    griddep_wait();               // x may come from the kernel this launch overlaps
+    griddep_launch_dependents();  // the next kernel waits for this one's completion before reading
     const T* xr = x + (size_t)blockIdx.x * n;
     T* yr = y + (size_t)blockIdx.x * n;
     float s = 0.f;
@@ -45,6 +47,8 @@ template <typename T, int PER>
 __global__ void __launch_bounds__(kThreads) rms_norm_vec_kernel(const T* __restrict__ x, const T* __restrict__ res,
                                                                 const T* __restrict__ w, T* __restrict__ s_out,
                                                                 T* __restrict__ y, int n, float eps) {
+    griddep_wait();
+    griddep_launch_dependents();
     constexpr int VEC = 16 / sizeof(T);
     const int nvec = n / VEC;
     const size_t row = (size_t)blockIdx.x * n;
@@ -105,6 +109,8 @@ __global__ void __launch_bounds__(kThreads) rms_norm_vec_kernel(const T* __restr
 // product in float32 rounded once.
 template <typename T>
 __global__ void silu_mul_kernel(const T* __restrict__ gu, T* __restrict__ y, long long rows, int n) {
+    griddep_wait();
+    griddep_launch_dependents();
     const long long total = rows * n;
     for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
          idx += (long long)gridDim.x * blockDim.x) {
@@ -129,6 +135,8 @@ template <typename T, int XR, int ROWS>
 __global__ void __launch_bounds__(GV_THREADS, XR == 1 ? 2 : 1) gemv_kernel(const T* __restrict__ w,
                                                                            const T* __restrict__ x,
                                                                            T* __restrict__ y, int N, int K, int xrows) {
+    griddep_wait();
+    griddep_launch_dependents();
     extern __shared__ float4 xs4[];  // [xrows][K / 4]
     float* xs = reinterpret_cast<float*>(xs4);
     for (int i = threadIdx.x; i < xrows * K; i += GV_THREADS) xs[i] = to_f32<T>(x[i]);
@@ -203,16 +211,16 @@ rfsn_status rms_norm_launch(const void* x, const void* res, const void* w, void*
                            reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(s_out) |
                            reinterpret_cast<uintptr_t>(y)) & 15) == 0;
     if (aligned && n % VEC == 0 && n / VEC <= kThreads * kVecPer) {
-        rms_norm_vec_kernel<T, kVecPer><<<rows, kThreads, 0, s>>>(
-            static_cast<const T*>(x), static_cast<const T*>(res), static_cast<const T*>(w), static_cast<T*>(s_out),
-            static_cast<T*>(y), n, eps);
+        RFSN_CUDA(launch_pdl(rms_norm_vec_kernel<T, kVecPer>, dim3(rows), dim3(kThreads), 0, s,
+                             static_cast<const T*>(x), static_cast<const T*>(res), static_cast<const T*>(w),
+                             static_cast<T*>(s_out), static_cast<T*>(y), n, eps));
     } else {
         if (res != nullptr) {
             set_error("rfsn_rms_norm: a residual needs 16-byte aligned rows of at most %d vectors", kThreads * kVecPer);
             return RFSN_ERR_UNSUPPORTED;
         }
-        rms_norm_kernel<T><<<rows, kThreads, 0, s>>>(static_cast<const T*>(x), static_cast<const T*>(w),
-                                                     static_cast<T*>(y), n, eps);
+        RFSN_CUDA(launch_pdl(rms_norm_kernel<T>, dim3(rows), dim3(kThreads), 0, s, static_cast<const T*>(x),
+                             static_cast<const T*>(w), static_cast<T*>(y), n, eps));
     }
     RFSN_CUDA(cudaGetLastError());
     note_launch();
@@ -225,8 +233,8 @@ rfsn_status gemv_launch_rows(const void* w, const void* x, void* y, int N, int K
     const size_t smem = sizeof(float) * (size_t)xrows * K;
     auto kern = gemv_kernel<T, XR, ROWS>;
     RFSN_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    kern<<<blocks, GV_THREADS, smem, s>>>(static_cast<const T*>(w), static_cast<const T*>(x), static_cast<T*>(y), N, K,
-                                          xrows);
+    RFSN_CUDA(launch_pdl(kern, dim3(blocks), dim3(GV_THREADS), smem, s, static_cast<const T*>(w),
+                         static_cast<const T*>(x), static_cast<T*>(y), N, K, xrows));
     RFSN_CUDA(cudaGetLastError());
     note_launch();
     return RFSN_OK;
@@ -262,7 +270,8 @@ rfsn_status silu_mul_launch(const void* gu, void* y, int rows, int n, cudaStream
     const long long total = (long long)rows * n;
     long long blocks = (total + kThreads - 1) / kThreads;
     if (blocks > 148LL * 16) blocks = 148LL * 16;
-    silu_mul_kernel<T><<<(unsigned)blocks, kThreads, 0, s>>>(static_cast<const T*>(gu), static_cast<T*>(y), rows, n);
+    RFSN_CUDA(launch_pdl(silu_mul_kernel<T>, dim3((unsigned)blocks), dim3(kThreads), 0, s,
+                         static_cast<const T*>(gu), static_cast<T*>(y), (long long)rows, n));
     RFSN_CUDA(cudaGetLastError());
     note_launch();
     return RFSN_OK;

@@ -20,8 +20,10 @@ __global__ void rope_append_kernel(const TIn* __restrict__ q, const TIn* __restr
     // A decode kernel launched after this one under programmatic dependent
     // launch may start now: before its dependency wait it only reads archived
     // arena rows, which this kernel never writes (it writes ring rows, q_out
-    // and the state copy, all read after that wait).
+    // and the state copy, all read after that wait). This kernel is itself
+    // launched that way and reads its inputs after its own wait.
     griddep_launch_dependents();
+    griddep_wait();  // its inputs may come from the kernel this launch overlaps
     const int half = head_dim >> 1;
     const long q_rows = (long)batch * q_heads * len;
     const long kv_rows = (long)batch * kv_heads * len;
@@ -111,10 +113,11 @@ rfsn_status rope_append_launch(int dtype, const void* q, const void* k, const vo
     if (blocks > 65535L * 8) blocks = 65535L * 8;
     if (blocks < 1) blocks = 1;
 #define RFSN_ROPE_LAUNCH(T)                                                                                     \
-    ring::rope_append_kernel<T, T><<<(unsigned)blocks, threads, 0, stream>>>(                                   \
-        static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(v), inv_freq, pos0, batch,    \
-        q_heads, kv_heads, len, head_dim, q_out, static_cast<T*>(ak), static_cast<T*>(av), rows, ring_row0,     \
-        capacity, write_index, step_state, step_state_copy)
+    RFSN_CUDA(launch_pdl(ring::rope_append_kernel<T, T>, dim3((unsigned)blocks), dim3(threads), 0, stream,        \
+                         static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(v), inv_freq,  \
+                         pos0, batch, q_heads, kv_heads, len, head_dim, q_out, static_cast<T*>(ak),              \
+                         static_cast<T*>(av), rows, ring_row0, capacity, write_index, step_state,                 \
+                         step_state_copy))
     if (dtype == RFSN_F32) {
         RFSN_ROPE_LAUNCH(float);
     } else if (dtype == RFSN_F16) {

@@ -81,6 +81,7 @@ def _no_alloc(c, layout):
         ("bfloat16", 1, 32, 8, 1, 128, [1000] * 12 + [24]),  # tensor-core kernel
         ("float16", 1, 32, 8, 1, 128, [256] * 6),
         ("float32", 1, 4, 2, 3, 64, [37, 64, 5]),              # CUDA-core kernel
+        ("float16", 1, 32, 8, 1024, 128, [64, 64]),            # tensor-core prefill: no partials when unsplit
     ],
 )
 def test_noalloc_matches_workspace_entry_point_twice(dtype, B, H, Hkv, Lq, D, blocks):
@@ -101,8 +102,9 @@ def test_noalloc_matches_workspace_entry_point_twice(dtype, B, H, Hkv, Lq, D, bl
 def test_noalloc_rejects_shapes_beyond_its_scratch():
     from rfsn_b200 import _native as native
 
-    # 1024 query rows x 4 heads per KV head: the split partials alone exceed the built-in array.
-    layout = make_layout("float16", 1, 8, 128, [64, 64], 2048, 1024, 0, seed=22)
+    # 1024 query rows x 4 heads per KV head on the CUDA-core kernel (float32 K/V):
+    # its per-row partials alone exceed the built-in array.
+    layout = make_layout("float32", 1, 8, 128, [64, 64], 2048, 1024, 0, seed=22)
     q = np.zeros((1, 32, 1024, 128), np.float32)
     c = _device_case(layout, q)
     status, _, _ = _no_alloc(c, layout)
