@@ -201,6 +201,31 @@ __global__ void __launch_bounds__(GV_THREADS, XR == 1 ? 2 : 1) gemv_kernel(const
     }
 }
 
+// The same, 16-byte vectors per thread (n a multiple of the vector width,
+// 16-byte aligned rows, fewer than 2^31 vectors).
+template <typename T>
+__global__ void silu_mul_vec_kernel(const T* __restrict__ gu, T* __restrict__ y, int total_vec, int nvec) {
+    griddep_wait();
+    griddep_launch_dependents();
+    constexpr int VEC = 16 / sizeof(T);
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total_vec; i += gridDim.x * blockDim.x) {
+        const int r = i / nvec, c = i - r * nvec;
+        const uint4 gv = reinterpret_cast<const uint4*>(gu)[(size_t)r * 2 * nvec + c];
+        const uint4 uv = reinterpret_cast<const uint4*>(gu)[(size_t)r * 2 * nvec + nvec + c];
+        const T* g = reinterpret_cast<const T*>(&gv);
+        const T* u = reinterpret_cast<const T*>(&uv);
+        uint4 ov;
+        T* o = reinterpret_cast<T*>(&ov);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) {
+            const float gf = to_f32<T>(g[e]);
+            const float s = to_f32<T>(from_f32<T>(gf / (1.f + expf(-gf))));
+            o[e] = from_f32<T>(s * to_f32<T>(u[e]));
+        }
+        reinterpret_cast<uint4*>(y)[i] = ov;
+    }
+}
+
 constexpr int kVecPer = 4;  // vectors per thread held in registers: rows up to 8192 bf16 / 4096 fp32 elements
 
 template <typename T>
@@ -267,6 +292,17 @@ rfsn_status gemv_launch(const void* w, const void* x, void* y, int N, int K, int
 
 template <typename T>
 rfsn_status silu_mul_launch(const void* gu, void* y, int rows, int n, cudaStream_t s) {
+    constexpr int VEC = 16 / sizeof(T);
+    const long long total_vec = (long long)rows * (n / VEC);
+    if (n % VEC == 0 && ((reinterpret_cast<uintptr_t>(gu) | reinterpret_cast<uintptr_t>(y)) & 15) == 0 &&
+        total_vec < (1LL << 31)) {
+        long long blocks = (total_vec + kThreads - 1) / kThreads;
+        if (blocks > 148LL * 8) blocks = 148LL * 8;
+        RFSN_CUDA(launch_pdl(silu_mul_vec_kernel<T>, dim3((unsigned)blocks), dim3(kThreads), 0, s,
+                             static_cast<const T*>(gu), static_cast<T*>(y), (int)total_vec, n / VEC));
+        note_launch();
+        return RFSN_OK;
+    }
     const long long total = (long long)rows * n;
     long long blocks = (total + kThreads - 1) / kThreads;
     if (blocks > 148LL * 16) blocks = 148LL * 16;
@@ -301,6 +337,9 @@ void preload_model_kernels() {
     preload_gemv<float>();
     preload_gemv<__half>();
     preload_gemv<__nv_bfloat16>();
+    cudaFuncGetAttributes(&a, model_ops::silu_mul_vec_kernel<float>);
+    cudaFuncGetAttributes(&a, model_ops::silu_mul_vec_kernel<__half>);
+    cudaFuncGetAttributes(&a, model_ops::silu_mul_vec_kernel<__nv_bfloat16>);
     cudaFuncGetAttributes(&a, model_ops::silu_mul_kernel<float>);
     cudaFuncGetAttributes(&a, model_ops::silu_mul_kernel<__half>);
     cudaFuncGetAttributes(&a, model_ops::silu_mul_kernel<__nv_bfloat16>);
