@@ -105,24 +105,104 @@ def _layer_norm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: 
     return F.layer_norm(x.float(), (x.shape[-1],), weight.float(), bias.float(), eps).to(x.dtype)
 
 
-class RFSNLayer:
-    """One transformer layer (layer.py:67-167) with the attention step on the CUDA path."""
+def _layer_param_shapes(config: RFSNConfig, layer_idx: int) -> Dict[str, Tuple[int, ...]]:
+    Hd, H, Hkv, D, Fd = config.hidden_dim, config.num_heads, config.num_kv_heads, config.head_dim, config.ffn_dim
+    pre = f"layers.{layer_idx}."
+    return {
+        pre + "q_proj.weight": (H * D, Hd), pre + "k_proj.weight": (Hkv * D, Hd),
+        pre + "v_proj.weight": (Hkv * D, Hd), pre + "o_proj.weight": (Hd, H * D),
+        pre + "gate_proj.weight": (Fd, Hd), pre + "up_proj.weight": (Fd, Hd),
+        pre + "down_proj.weight": (Hd, Fd),
+        pre + "attn_norm.weight": (Hd,), pre + "ffn_norm.weight": (Hd,),
+    }
 
-    def __init__(self, config: RFSNConfig, layer_idx: int, params: Dict[str, torch.Tensor],
-                 w_qkv: torch.Tensor, w_gate_up: torch.Tensor) -> None:
+
+def _fused_layer_storage(config: RFSNConfig, layer_idx: int, params: Dict[str, torch.Tensor], device: torch.device,
+                         dtype: torch.dtype) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Allocate one layer's q|k|v and gate|up matrices and register the named
+    projection parameters as row views of them."""
+    H, Hkv, D, Hd, Fd = config.num_heads, config.num_kv_heads, config.head_dim, config.hidden_dim, config.ffn_dim
+    pre = f"layers.{layer_idx}."
+    w_qkv = torch.empty(((H + 2 * Hkv) * D, Hd), device=device, dtype=dtype)
+    w_gu = torch.empty((2 * Fd, Hd), device=device, dtype=dtype)
+    params[pre + "q_proj.weight"] = w_qkv[:H * D]
+    params[pre + "k_proj.weight"] = w_qkv[H * D:(H + Hkv) * D]
+    params[pre + "v_proj.weight"] = w_qkv[(H + Hkv) * D:]
+    params[pre + "gate_proj.weight"] = w_gu[:Fd]
+    params[pre + "up_proj.weight"] = w_gu[Fd:]
+    return w_qkv, w_gu
+
+
+def _init_params(shapes: Mapping[str, Tuple[int, ...]], params: Dict[str, torch.Tensor], device: torch.device,
+                 dtype: torch.dtype, gen: torch.Generator) -> None:
+    """Random init normal(0, 0.02) in ``shapes`` order (norms: ones / zeros),
+    written into existing views or stored as new tensors."""
+    for name, shape in shapes.items():
+        if name.endswith("norm.weight"):
+            t = torch.ones(shape, device=device, dtype=dtype)
+        elif name == "norm.bias":
+            t = torch.zeros(shape, device=device, dtype=dtype)
+        else:
+            t = torch.empty(shape, device=device, dtype=torch.float32).normal_(0.0, 0.02, generator=gen).to(dtype)
+        if name in params:
+            params[name].copy_(t)
+        else:
+            params[name] = t
+
+
+class _Weight:
+    """A projection or norm of the layer with the reference module's
+    ``.weight`` attribute (a view of the layer's parameter)."""
+
+    __slots__ = ("weight",)
+
+    def __init__(self, weight: torch.Tensor) -> None:
+        self.weight = weight
+
+
+class RFSNLayer:
+    """One transformer layer (layer.py:67-167) with the attention step on the CUDA path.
+
+    ``RFSNLayer(config, layer_idx)`` (the reference's ``RFSNLayerMLX``
+    constructor) builds a standalone layer with its own parameters, drawn
+    normal(0, 0.02) (norms ones) on ``device`` (default: the current CUDA
+    device); the model passes its parameter dict and fused matrices instead.
+    The reference's ``q_proj`` ... ``down_proj``, ``attn_norm`` and
+    ``ffn_norm`` attributes expose ``.weight`` views of the parameters."""
+
+    def __init__(self, config: RFSNConfig, layer_idx: int, params: Optional[Dict[str, torch.Tensor]] = None,
+                 w_qkv: Optional[torch.Tensor] = None, w_gate_up: Optional[torch.Tensor] = None, *,
+                 device: Optional[Union[str, torch.device]] = None, seed: Optional[int] = None) -> None:
         self.config = config
         self.layer_idx = layer_idx
-        self.p = params  # the model's parameter dict
+        if params is None:
+            dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+            dtype = resolve_dtype(config.model_dtype)
+            params = {}
+            w_qkv, w_gate_up = _fused_layer_storage(config, layer_idx, params, dev, dtype)
+            gen = torch.Generator(device=dev)
+            gen.manual_seed(layer_idx if seed is None else seed)
+            _init_params(_layer_param_shapes(config, layer_idx), params, dev, dtype, gen)
+        elif w_qkv is None or w_gate_up is None:
+            raise ValueError("a layer built from a parameter dict needs its fused q|k|v and gate|up matrices")
+        self.p = params  # the model's (or the layer's own) parameter dict
         # q|k|v and gate|up projections stored as one matrix each (the named
         # parameters are views of their rows): one GEMV instead of three / two
         self.w_qkv = w_qkv
         self.w_gate_up = w_gate_up
+        for name in ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj", "attn_norm",
+                     "ffn_norm"):
+            setattr(self, name, _Weight(self._w(f"{name}.weight")))
 
     def _w(self, name: str) -> torch.Tensor:
         return self.p[f"layers.{self.layer_idx}.{name}"]
 
-    def __call__(self, x: torch.Tensor, layer_cache, start_pos: int, attn=None) -> torch.Tensor:
-        """``attn(q, k, v)`` replaces the attention step (used by the captured decode graph)."""
+    def __call__(self, x: torch.Tensor, cache, rope_tables=None, start_pos: int = 0, attn=None) -> torch.Tensor:
+        """layer.py:97-167. ``rope_tables`` is accepted for the reference's call
+        signature; the rotation is computed in the fused RoPE/append kernel from
+        the cache's frequency table. ``attn(q, k, v)`` replaces the attention
+        step (used by the captured decode graph)."""
+        layer_cache = cache
         cfg = self.config
         B, L, _ = x.shape
         H, Hkv, D = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
@@ -153,30 +233,9 @@ class RFSNModel:
         # model initialises in seconds); norms start at ones / zeros
         gen = torch.Generator(device=self.device)
         gen.manual_seed(0 if seed is None else seed)
-        Hd, H, Hkv, D, Fd = config.hidden_dim, config.num_heads, config.num_kv_heads, config.head_dim, config.ffn_dim
-        fused = []
-        for i in range(config.num_layers):  # the fused matrices own the q/k/v and gate/up rows
-            pre = f"layers.{i}."
-            w_qkv = torch.empty(((H + 2 * Hkv) * D, Hd), device=self.device, dtype=self.dtype)
-            w_gu = torch.empty((2 * Fd, Hd), device=self.device, dtype=self.dtype)
-            self.params[pre + "q_proj.weight"] = w_qkv[:H * D]
-            self.params[pre + "k_proj.weight"] = w_qkv[H * D:(H + Hkv) * D]
-            self.params[pre + "v_proj.weight"] = w_qkv[(H + Hkv) * D:]
-            self.params[pre + "gate_proj.weight"] = w_gu[:Fd]
-            self.params[pre + "up_proj.weight"] = w_gu[Fd:]
-            fused.append((w_qkv, w_gu))
-        for name, shape in self.parameter_shapes().items():
-            if name.endswith("norm.weight"):
-                t = torch.ones(shape, device=self.device, dtype=self.dtype)
-            elif name == "norm.bias":
-                t = torch.zeros(shape, device=self.device, dtype=self.dtype)
-            else:
-                t = torch.empty(shape, device=self.device, dtype=torch.float32).normal_(0.0, 0.02, generator=gen)
-                t = t.to(self.dtype)
-            if name in self.params:
-                self.params[name].copy_(t)
-            else:
-                self.params[name] = t
+        # the fused matrices own the q/k/v and gate/up rows
+        fused = [_fused_layer_storage(config, i, self.params, self.device, self.dtype) for i in range(config.num_layers)]
+        _init_params(self.parameter_shapes(), self.params, self.device, self.dtype, gen)
         self.layers = [RFSNLayer(config, i, self.params, *fused[i]) for i in range(config.num_layers)]
         self.use_graphs = True
         self._graph: Optional["_DecodeGraph"] = None
@@ -184,17 +243,10 @@ class RFSNModel:
     # ------------------------------------------------------------------ parameters
     def parameter_shapes(self) -> Dict[str, Tuple[int, ...]]:
         cfg = self.config
-        Hd, H, Hkv, D, Fd = cfg.hidden_dim, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, cfg.ffn_dim
+        Hd = cfg.hidden_dim
         shapes = {"embed_tokens.weight": (cfg.vocab_size, Hd), "norm.weight": (Hd,), "norm.bias": (Hd,)}
         for i in range(cfg.num_layers):
-            pre = f"layers.{i}."
-            shapes.update({
-                pre + "q_proj.weight": (H * D, Hd), pre + "k_proj.weight": (Hkv * D, Hd),
-                pre + "v_proj.weight": (Hkv * D, Hd), pre + "o_proj.weight": (Hd, H * D),
-                pre + "gate_proj.weight": (Fd, Hd), pre + "up_proj.weight": (Fd, Hd),
-                pre + "down_proj.weight": (Hd, Fd),
-                pre + "attn_norm.weight": (Hd,), pre + "ffn_norm.weight": (Hd,),
-            })
+            shapes.update(_layer_param_shapes(cfg, i))
         return shapes
 
     def parameters(self) -> Dict[str, torch.Tensor]:
@@ -266,7 +318,7 @@ class RFSNModel:
     def _forward(self, x: torch.Tensor, cache: RFSNCache, start_pos: int) -> torch.Tensor:
         """model.py:106-131."""
         for i, layer in enumerate(self.layers):
-            x = layer(x, cache.layer(i), start_pos)
+            x = layer(x, cache.layer(i), start_pos=start_pos)
         x = _layer_norm(x, self.params["norm.weight"], self.params["norm.bias"], self.config.norm_eps)
         return self._lm_head(x)
 
@@ -459,7 +511,7 @@ class _DecodeGraph:
         x = F.embedding(self.tok.view(-1, 1), model.params["embed_tokens.weight"])
         for i, layer in enumerate(model.layers):
             lc, sg = cache.layer(i), segs[i]
-            x = layer(x, lc, 0, attn=lambda q, k, v, lc=lc, sg=sg: self._attention(lc, sg, q, k, v))
+            x = layer(x, lc, attn=lambda q, k, v, lc=lc, sg=sg: self._attention(lc, sg, q, k, v))
         x = _layer_norm(x, model.params["norm.weight"], model.params["norm.bias"], model.config.norm_eps)
         return model._lm_head(x)[:, 0, :]
 
@@ -497,4 +549,5 @@ class _DecodeGraph:
         self.logits.copy_(logits)
 
 
-RFSNMLX = RFSNModel  # the reference's class name
+RFSNMLX = RFSNModel  # the reference's class names
+RFSNLayerMLX = RFSNLayer

@@ -87,3 +87,23 @@ def test_greedy_and_sampling_rules():
     # a repetition penalty on the argmax (positive logit divided) can move the choice under top-k 1
     t = RFSNModel._sample(logits, 1.0, 1.0, 1, 100.0, torch.tensor([[1]]), gen)
     assert int(t[0]) == 3
+
+
+def test_standalone_layer_has_the_reference_surface(tmp_path):
+    """RFSNLayerMLX(config, layer_idx) builds a layer with its own parameters;
+    q/k/v and gate/up are row views of its fused matrices, exposed through the
+    reference's ``.weight`` attributes."""
+    import torch
+
+    from rfsn_b200 import RFSNLayerMLX
+
+    cfg = tiny_config(tmp_path)
+    layer = RFSNLayerMLX(cfg, 0, device="cpu")
+    H, Hkv, D, Hd, Fd = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, cfg.hidden_dim, cfg.ffn_dim
+    assert tuple(layer.q_proj.weight.shape) == (H * D, Hd)
+    assert tuple(layer.k_proj.weight.shape) == (Hkv * D, Hd)
+    assert tuple(layer.down_proj.weight.shape) == (Hd, Fd)
+    assert torch.equal(layer.attn_norm.weight, torch.ones(Hd, dtype=layer.attn_norm.weight.dtype))
+    layer.k_proj.weight.fill_(0.5)  # a write through the reference attribute lands in the fused matrix
+    assert bool((layer.w_qkv[H * D:(H + Hkv) * D] == 0.5).all())
+    assert layer.up_proj.weight.data_ptr() == layer.w_gate_up[Fd:].data_ptr()

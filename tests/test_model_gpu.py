@@ -314,3 +314,29 @@ def test_decode_gemv_matches_float32_product(dtype, rows, n, k):
     got = _linear(x, w).float()
     tol = {torch.float32: 1e-4, torch.bfloat16: 1.6e-2, torch.float16: 2e-3}[dtype]
     assert torch.allclose(got, want, rtol=tol, atol=tol * float(want.abs().max())), float((got - want).abs().max())
+
+
+def test_standalone_layer_matches_the_model_layer(tmp_path):
+    """RFSNLayerMLX(config, 0) with the model's layer-0 weights, called with the
+    reference's positional signature (x, cache, rope_tables, start_pos), gives
+    the model layer's output and cache state."""
+    from rfsn_b200 import RFSNCache, RFSNLayerMLX, RFSNModel
+
+    cfg = tiny_config(tmp_path / "a")
+    model = RFSNModel(cfg, device="cuda", seed=3)
+    layer = RFSNLayerMLX(cfg, 0, device="cuda")
+    for name in ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj", "attn_norm",
+                 "ffn_norm"):
+        getattr(layer, name).weight.copy_(getattr(model.layers[0], name).weight)
+    c1 = RFSNCache(cfg, batch_size=1, device="cuda")
+    c2 = RFSNCache(tiny_config(tmp_path / "b"), batch_size=1, device="cuda")
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    pos = 0
+    for L in (6, 1, 1, 5):  # prefill-like chunks and decode steps across seals of the 8-token ring
+        x = torch.randn((1, L, cfg.hidden_dim), generator=gen, device="cuda")
+        a = model.layers[0](x, c1.layer(0), start_pos=pos)
+        b = layer(x, c2.layer(0), None, pos)
+        assert torch.equal(a, b)
+        pos += L
+    l1, l2 = c1.layer(0), c2.layer(0)
+    assert (l1.hot_head_index, l1.hot_seq_len, l1.hot_start) == (l2.hot_head_index, l2.hot_seq_len, l2.hot_start)
