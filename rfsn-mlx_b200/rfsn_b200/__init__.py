@@ -22,7 +22,7 @@ from .attention_exact import (  # noqa: F401
     run_segmented_attention,
 )
 from .layer import GraphedDecodeStep, attention_step, build_rope_tables  # noqa: F401
-from .model import RFSNMLX, RFSNLayer, RFSNLayerMLX, RFSNModel  # noqa: F401
+from .model import RFSNMLX, RFSNLayer, RFSNLayerMLX, RFSNLayerNorm, RFSNModel  # noqa: F401
 
 __all__ = [
     "RFSNConfig",

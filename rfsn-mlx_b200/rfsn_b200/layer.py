@@ -194,3 +194,14 @@ class GraphedDecodeStep:
         self.replays += 1
         torch.cuda.current_stream().synchronize()
         return self.out_host
+
+
+def __getattr__(name: str):
+    """The reference's ``layer`` module also holds the layer and its RMS norm
+    (``RFSNLayerMLX``, ``RFSNLayerNorm``); they live in ``model`` here and
+    are resolved on first use (``model`` imports this module)."""
+    if name in ("RFSNLayerMLX", "RFSNLayerNorm", "RFSNLayer"):
+        from . import model
+
+        return getattr(model, name)
+    raise AttributeError(f"module {__name__!r} has no attribute {name!r}")

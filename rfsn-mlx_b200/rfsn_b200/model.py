@@ -151,13 +151,34 @@ def _init_params(shapes: Mapping[str, Tuple[int, ...]], params: Dict[str, torch.
 
 
 class _Weight:
-    """A projection or norm of the layer with the reference module's
-    ``.weight`` attribute (a view of the layer's parameter)."""
+    """A projection of the layer with the reference module's ``.weight``
+    attribute (a view of the layer's parameter)."""
 
     __slots__ = ("weight",)
 
     def __init__(self, weight: torch.Tensor) -> None:
         self.weight = weight
+
+
+class RFSNLayerNorm:
+    """layer.py:53-64 RMS norm (no bias): ``weight`` (ones unless given) and
+    ``eps``; ``norm(x)`` is weight * x / sqrt(mean(x^2) + eps) computed in float32
+    by the fused kernel and returned in x's dtype (the weight is read in x's
+    dtype)."""
+
+    def __init__(self, dim: int, eps: float = 1e-5, *, weight: Optional[torch.Tensor] = None,
+                 device: Optional[Union[str, torch.device]] = None, dtype: torch.dtype = torch.float32) -> None:
+        if weight is None:
+            dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+            weight = torch.ones((dim,), device=dev, dtype=dtype)
+        if tuple(weight.shape) != (dim,):
+            raise ValueError(f"RMS norm weight must have shape ({dim},), got {tuple(weight.shape)}")
+        self.weight = weight
+        self.eps = eps
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        w = self.weight if self.weight.dtype == x.dtype else self.weight.to(x.dtype)
+        return _rms_norm(x, w, self.eps)
 
 
 class RFSNLayer:
@@ -190,9 +211,10 @@ class RFSNLayer:
         # parameters are views of their rows): one GEMV instead of three / two
         self.w_qkv = w_qkv
         self.w_gate_up = w_gate_up
-        for name in ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj", "attn_norm",
-                     "ffn_norm"):
+        for name in ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj"):
             setattr(self, name, _Weight(self._w(f"{name}.weight")))
+        self.attn_norm = RFSNLayerNorm(config.hidden_dim, config.norm_eps, weight=self._w("attn_norm.weight"))
+        self.ffn_norm = RFSNLayerNorm(config.hidden_dim, config.norm_eps, weight=self._w("ffn_norm.weight"))
 
     def _w(self, name: str) -> torch.Tensor:
         return self.p[f"layers.{self.layer_idx}.{name}"]

@@ -104,6 +104,9 @@ def test_standalone_layer_has_the_reference_surface(tmp_path):
     assert tuple(layer.k_proj.weight.shape) == (Hkv * D, Hd)
     assert tuple(layer.down_proj.weight.shape) == (Hd, Fd)
     assert torch.equal(layer.attn_norm.weight, torch.ones(Hd, dtype=layer.attn_norm.weight.dtype))
+    from rfsn_b200.layer import RFSNLayerMLX as from_layer_module, RFSNLayerNorm
+
+    assert from_layer_module is RFSNLayerMLX and isinstance(layer.ffn_norm, RFSNLayerNorm)
     layer.k_proj.weight.fill_(0.5)  # a write through the reference attribute lands in the fused matrix
     assert bool((layer.w_qkv[H * D:(H + Hkv) * D] == 0.5).all())
     assert layer.up_proj.weight.data_ptr() == layer.w_gate_up[Fd:].data_ptr()
