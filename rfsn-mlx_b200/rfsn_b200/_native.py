@@ -342,6 +342,9 @@ _workspaces: dict[int, Workspace] = {}
 
 
 def default_workspace(device: torch.device) -> Workspace:
+    """The per-device workspace of calls that pass none. Its arrival counters
+    are shared, so attention calls that may run concurrently (on different
+    streams) must each pass their own ``Workspace``."""
     idx = device.index if device.index is not None else torch.cuda.current_device()
     ws = _workspaces.get(idx)
     if ws is None:
