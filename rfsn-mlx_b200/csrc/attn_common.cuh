@@ -171,37 +171,62 @@ __device__ __forceinline__ void peer_store_and_merge(const PeerParams& peer, con
     }
     const uint2* local = peer.words[peer.rank] + (size_t)(call & 1) * half + ((size_t)group * kPeerSlots + sl) * slot_words;
     const size_t src_stride = (size_t)groups * kPeerSlots * slot_words;
+    // Sources are polled two at a time: the words of a group are requested
+    // together (one round trip per poll instead of one per rank), and the
+    // sources that have not arrived are polled again. Merged in rank order.
+    constexpr int kGroup = 2;  // the load results of a group stay in registers (no spill at 2 CTAs per SM)
     const long long t0 = global_ns();
     bool timed_out = false;
     // online merge in rank order: running max M, weight sum W, weighted sum acc
     float M = -CUDART_INF_F, W = 0.f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int src = 0; src < P; ++src) {
-        const uint2* w = local + src * src_stride;
-        uint4 a, b, l;
+    for (int g0 = 0; g0 < P && !timed_out; g0 += kGroup) {
+        const int n = min(kGroup, P - g0);
+        const unsigned want = (1u << n) - 1u;
+        unsigned ready = 0;
+        uint4 a[kGroup], b[kGroup], l[kGroup];
+#pragma unroll
+        for (int s = 0; s < kGroup; ++s) a[s] = b[s] = l[s] = make_uint4(0, 0, 0, 0);
         for (;;) {
-            a = ld_volatile_v4(w + 4 * d4);
-            b = ld_volatile_v4(w + 4 * d4 + 2);
-            l = ld_volatile_v4(w + head_dim);
-            if (a.y == stamp && a.w == stamp && b.y == stamp && b.w == stamp && l.y == stamp) break;
-            if (timed_out || global_ns() - t0 > peer.timeout_ns) {
+#pragma unroll
+            for (int s = 0; s < kGroup; ++s) {
+                if (s < n && !((ready >> s) & 1u)) {
+                    const uint2* w = local + (g0 + s) * src_stride;
+                    a[s] = ld_volatile_v4(w + 4 * d4);
+                    b[s] = ld_volatile_v4(w + 4 * d4 + 2);
+                    l[s] = ld_volatile_v4(w + head_dim);
+                }
+            }
+#pragma unroll
+            for (int s = 0; s < kGroup; ++s) {
+                if (s < n && a[s].y == stamp && a[s].w == stamp && b[s].y == stamp && b[s].w == stamp &&
+                    l[s].y == stamp)
+                    ready |= 1u << s;
+            }
+            if (ready == want) break;
+            if (global_ns() - t0 > peer.timeout_ns) {
                 timed_out = true;
                 break;
             }
             __nanosleep(20);
         }
-        const float ls = __uint_as_float(l.x);
-        if (ls == -CUDART_INF_F) continue;  // a part that saw no visible key
-        const float4 v = make_float4(__uint_as_float(a.x), __uint_as_float(a.z), __uint_as_float(b.x), __uint_as_float(b.z));
-        if (ls > M) {
-            const float sc = (M == -CUDART_INF_F) ? 0.f : expf(M - ls);
-            W = W * sc + 1.f;
-            acc = make_float4(acc.x * sc + v.x, acc.y * sc + v.y, acc.z * sc + v.z, acc.w * sc + v.w);
-            M = ls;
-        } else {
-            const float wgt = expf(ls - M);
-            W += wgt;
-            acc = make_float4(acc.x + wgt * v.x, acc.y + wgt * v.y, acc.z + wgt * v.z, acc.w + wgt * v.w);
+#pragma unroll
+        for (int s = 0; s < kGroup; ++s) {
+            if (s >= n || !((ready >> s) & 1u)) continue;  // after a timeout only the parts that arrived
+            const float ls = __uint_as_float(l[s].x);
+            if (ls == -CUDART_INF_F) continue;  // a part that saw no visible key
+            const float4 v = make_float4(__uint_as_float(a[s].x), __uint_as_float(a[s].z), __uint_as_float(b[s].x),
+                                         __uint_as_float(b[s].z));
+            if (ls > M) {
+                const float sc = (M == -CUDART_INF_F) ? 0.f : expf(M - ls);
+                W = W * sc + 1.f;
+                acc = make_float4(acc.x * sc + v.x, acc.y * sc + v.y, acc.z * sc + v.z, acc.w * sc + v.w);
+                M = ls;
+            } else {
+                const float wgt = expf(ls - M);
+                W += wgt;
+                acc = make_float4(acc.x + wgt * v.x, acc.y + wgt * v.y, acc.z + wgt * v.z, acc.w + wgt * v.w);
+            }
         }
     }
     if (timed_out) atomicExch(ws.error, kDevErrPeerTimeout);
