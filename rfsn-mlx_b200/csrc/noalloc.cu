@@ -64,6 +64,11 @@ extern "C" rfsn_status rfsn_paged_attention_noalloc(const rfsn_arena* arena, con
                                                     int kv_heads, int q_len, int q_pos0, const rfsn_page_table* table,
                                                     const rfsn_hot_window* hot, float* out, float* lse, int max_splits,
                                                     void* stream) {
+    // Pointer arguments are rejected before the set-up and the counter clear,
+    // so a bad call issues no CUDA work at all.
+    RFSN_CHECK_ARG(arena != nullptr && table != nullptr && hot != nullptr,
+                   "rfsn_paged_attention_noalloc: NULL arena/table/hot");
+    RFSN_CHECK_ARG(q != nullptr && out != nullptr, "rfsn_paged_attention_noalloc: NULL q/out");
     void* scratch = nullptr;
     rfsn_status st = scratch_address(&scratch);
     if (st != RFSN_OK) return st;
