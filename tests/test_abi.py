@@ -72,3 +72,35 @@ def test_struct_layouts_match_header():
     assert ctypes.sizeof(native.PageTableC) == 24
     assert ctypes.sizeof(native.HotWindowC) == 32
     assert ctypes.sizeof(native.SegmentDescC) == 80
+
+
+def test_prefill_plan_invariants_over_random_shapes():
+    """The planner's answer is always a launchable split: 1-4 parts per split
+    unit, split units only at the end of the unit order, at most 4 parts per SM
+    and one arrival counter per split unit, the same answer for the same shape."""
+    hyp = pytest.importorskip("hypothesis")
+    st = hyp.strategies
+
+    @hyp.settings(max_examples=300, deadline=None, derandomize=True)
+    @hyp.given(batch=st.integers(1, 2), kv_heads=st.sampled_from([1, 2, 4, 8]), G=st.sampled_from([1, 2, 4, 8, 16]),
+               q_len=st.integers(64, 4096), archived=st.integers(0, 200_000), hot_len=st.integers(0, 8192),
+               back=st.integers(0, 8192))
+    def check(batch, kv_heads, G, q_len, archived, hot_len, back):
+        hot_start = archived
+        q_pos0 = hot_start + max(0, hot_len - min(back, hot_len))
+        whole, splits, ctas = native.prefill_plan(batch, G * kv_heads, kv_heads, q_len, q_pos0, archived, hot_start,
+                                                  hot_len)
+        ppc = 128 // G
+        units = -(-q_len // ppc) * batch * kv_heads
+        assert 1 <= splits <= 4 and 0 <= whole <= units
+        assert ctas == whole + (units - whole) * splits
+        if splits > 1:
+            assert units - whole >= 1
+            assert (units - whole) * splits <= 4 * 148  # 148 SMs (the host-side default without a device)
+            assert units - whole <= 16384
+        else:
+            assert ctas == units
+        assert native.prefill_plan(batch, G * kv_heads, kv_heads, q_len, q_pos0, archived, hot_start,
+                                   hot_len) == (whole, splits, ctas)
+
+    check()
