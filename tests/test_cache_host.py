@@ -195,3 +195,55 @@ def test_row_allocator_first_fit_and_coalescing():
     assert a.free == [[10, 30]]
     a.grow(40)
     assert a.allocate(30) == 10
+
+
+@pytest.mark.parametrize("seed", range(12))
+def test_random_append_sequences_match_ring_oracle(seed):
+    """Random chunk sequences (decode steps, ragged chunks, whole-ring chunks,
+    oversized chunks that must fail) through the drop-in cache and the ring
+    oracle: ring state, sealed block spans, segment order and every key/value
+    row agree after each step, bit for bit."""
+    import tempfile
+
+    import torch
+
+    from cache_replay import _config, _kv
+    from oracle.kv_ring import RingOracle
+    from rfsn_b200 import LayerKVCache
+
+    rng = np.random.default_rng(seed)
+    cap = int(rng.integers(2, 48))
+    bs = int(rng.integers(1, cap + 8))
+    with tempfile.TemporaryDirectory() as tmp:
+        cache = LayerKVCache(_config(cap, bs, "archived", 1 << 20, tmp), 1, 2, 1, layer_id=0, session_id="rand",
+                             ops=FakeDeviceOps())
+        ring = RingOracle(cap, bs)
+        pos = 0
+        for _ in range(40):
+            kind = rng.random()
+            n = 1 if kind < 0.4 else (cap if kind < 0.5 else (cap + 1 if kind < 0.55 else int(rng.integers(1, cap + 1))))
+            if n > cap:
+                with pytest.raises(RuntimeError) as err:
+                    cache.evict_for_append(n)
+                with pytest.raises(RuntimeError) as want:
+                    ring.evict_for_append(n)
+                assert str(err.value) == str(want.value)
+                continue
+            cache.evict_for_append(n)
+            ring.evict_for_append(n)
+            k, v = _kv(pos, n, cache.device)
+            cache.append_exact(k, v)
+            ring.append(n)
+            pos += n
+            assert (cache.hot_head_index, cache.hot_seq_len, cache.hot_start, cache.hot_write_index, cache.hot_end) == (
+                ring.head, ring.length, ring.start, ring.write_index, ring.end)
+            spans = [(m.logical_start, m.logical_end) for m in cache.block_manager.iter_blocks(layer_id=0)]
+            assert spans == ring.sealed
+            segs = cache.get_attention_segments()
+            want_segs = [(s, e - s) for s, e in ring.sealed] + [(s, n_) for _p, n_, s in ring.hot_spans()]
+            assert [(int(s[2]), int(s[0].shape[2])) for s in segs] == want_segs
+            assert cache.get_total_length() == pos
+            for kk, vv, start in segs:
+                expect = torch.arange(start, start + kk.shape[2], dtype=torch.float32)
+                assert torch.equal(kk[0, 0, :, 0].float().cpu(), expect)
+                assert torch.equal(vv[0, 0, :, 0].float().cpu(), expect + 0.5)
