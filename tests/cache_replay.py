@@ -9,7 +9,6 @@ from __future__ import annotations
 
 import tempfile
 
-import numpy as np
 import pytest
 import torch
 

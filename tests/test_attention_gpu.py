@@ -5,13 +5,10 @@ K/V with float32 accumulation). The paged kernels keep ~16 significand bits of
 q and p, so a tighter 1e-4 guard is also asserted to catch precision loss.
 """
 
-import ctypes
-
 import numpy as np
 import pytest
 
 from _util import golden_attention_cases, make_layout, run_paged
-from oracle.numerics import from_storage
 from oracle.segmented_attention import merge_partials, run_segmented_attention
 
 pytestmark = pytest.mark.gpu
