@@ -58,6 +58,11 @@ typedef int rfsn_status;
 /* Keys per attention tile. Page-table tile prefix sums are in these units. */
 #define RFSN_TILE_KEYS 64
 
+/* Every call returns an rfsn_status; on failure rfsn_last_error() describes it
+ * (kept per calling thread). The Python layer raises the reference's
+ * exception types for them: ValueError for bad arguments (config.py:88-129,
+ * model.py:77-99), RuntimeError for ring or scratch overflow
+ * (cache.py:345-375), TimeoutError for bounded waits. */
 RFSN_API const char* rfsn_last_error(void);
 RFSN_API int rfsn_abi_version(void);
 /* Number of SMs of the current device (used to size split-KV grids). */
@@ -111,8 +116,10 @@ typedef struct rfsn_hot_window {
 #define RFSN_STEP_START 4        /* hot_start after the append */
 #define RFSN_STEP_STATE_LEN 8
 
-/* One K/V arena pair of a layer; holds the TMA descriptors the decode kernel
- * streams tiles with. Created once per cache layer. The first arena created
+/* One K/V arena pair of a layer: the storage of the hot ring (hot_k / hot_v,
+ * cache.py:100-107) and of the archived block arrays that _seal_hot_prefix
+ * creates (cache.py:324-339), as rows of one buffer per K and V; holds the
+ * TMA descriptors the decode kernel streams tiles with. Created once per cache layer. The first arena created
  * on a device also loads every kernel of the library there (none is then
  * loaded lazily at its first launch, in the middle of a decode step). */
 typedef struct rfsn_arena rfsn_arena;
@@ -170,7 +177,7 @@ RFSN_API rfsn_status rfsn_rope_append_step(const void* q, const void* k, const v
 /* ------------------------------------------------------------------------
  * Dense-layer helpers of the model driver (not on the attention path).
  *
- * RMSNorm (layer.py:52-64): out = weight * x / sqrt(mean(x^2) + eps) per row
+ * RMSNorm (layer.py:54-64): out = weight * x / sqrt(mean(x^2) + eps) per row
  * of n elements, in float32, rounded to dtype once; x, weight and out share
  * the dtype (RFSN_F32 / F16 / BF16), rows are contiguous. With residual
  * (and sum_out) non-NULL the row is first s = x + residual rounded to dtype,
@@ -179,13 +186,14 @@ RFSN_API rfsn_status rfsn_rope_append_step(const void* q, const void* k, const v
 RFSN_API rfsn_status rfsn_rms_norm(const void* x, const void* residual, const void* weight, void* sum_out, void* out,
                                    int rows, int n, int dtype, float eps, void* stream);
 
-/* SwiGLU on a fused gate|up projection (layer.py:164-166): gate_up rows hold
+/* SwiGLU on a fused gate|up projection (layer.py:94-95): gate_up rows hold
  * [gate (n), up (n)]; out[r, c] = silu(gate[r, c]) * up[r, c], silu rounded to
  * dtype first, the product in float32 rounded once. */
 RFSN_API rfsn_status rfsn_silu_mul(const void* gate_up, void* out, int rows, int n, int dtype, void* stream);
 
 /* y[r, n] = sum_k weight[n, k] * x[r, k] for rows = 1..4 rows of x (a decode
- * token's projection; weight [n_out, k] row-major, 16-byte aligned rows),
+ * token's q|k|v, o, gate|up or down projection, layer.py:82-89; weight
+ * [n_out, k] row-major, 16-byte aligned rows),
  * float32 accumulation, y [rows, n_out] rounded to dtype once. */
 RFSN_API rfsn_status rfsn_gemv(const void* weight, const void* x, void* y, int n_out, int k, int rows, int dtype,
                                void* stream);

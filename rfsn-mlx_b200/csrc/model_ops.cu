@@ -7,7 +7,7 @@ namespace model_ops {
 
 constexpr int kThreads = 256;
 
-// layer.py:52-64: y = weight * x / sqrt(mean(x^2) + eps) in float32, rounded
+// layer.py:54-64: y = weight * x / sqrt(mean(x^2) + eps) in float32, rounded
 // to the storage type once. One CTA per row.
 template <typename T>
 __global__ void __launch_bounds__(kThreads) rms_norm_kernel(const T* __restrict__ x, const T* __restrict__ w,
@@ -104,7 +104,7 @@ __global__ void __launch_bounds__(kThreads) rms_norm_vec_kernel(const T* __restr
     }
 }
 
-// layer.py:164-166 SwiGLU on a fused gate|up projection row [2n]: y = silu(g) * u,
+// layer.py:94-95 SwiGLU on a fused gate|up projection row [2n]: y = silu(g) * u,
 // silu rounded to the storage type first (as an elementwise op would), the
 // product in float32 rounded once.
 template <typename T>

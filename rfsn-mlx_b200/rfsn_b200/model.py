@@ -42,7 +42,7 @@ def _dense_device_check(x: torch.Tensor) -> None:
 
 
 def _rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
-    """layer.py:52-64: weight * x / sqrt(mean(x^2) + eps), computed in float32
+    """layer.py:54-64: weight * x / sqrt(mean(x^2) + eps), computed in float32
     and rounded once (one fused kernel, ``rfsn_rms_norm``)."""
     _dense_device_check(x)
     xc = x.contiguous()
@@ -89,7 +89,7 @@ def _linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
 
 
 def _silu_mul(gate_up: torch.Tensor) -> torch.Tensor:
-    """layer.py:164-166 on a fused gate|up projection [..., 2F]: silu(gate) * up
+    """layer.py:94-95 on a fused gate|up projection [..., 2F]: silu(gate) * up
     (one kernel, ``rfsn_silu_mul``)."""
     _dense_device_check(gate_up)
     gu = gate_up.contiguous()

@@ -273,7 +273,7 @@ def test_decode_graph_falls_back_when_blocks_are_cold(tmp_path):
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 def test_fused_rms_norm_and_swiglu_match_the_elementwise_formulas(dtype):
     """rfsn_rms_norm / rfsn_silu_mul against the reference's elementwise
-    formulas (layer.py:52-64, :164-166) evaluated in torch: equal up to one
+    formulas (layer.py:54-64, :94-95) evaluated in torch: equal up to one
     rounding of the storage type (different summation order of the mean)."""
     from rfsn_b200.model import _add_rms_norm, _rms_norm, _silu_mul
 
