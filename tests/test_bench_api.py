@@ -53,3 +53,37 @@ def test_cli_bench_runs(tmp_path, capsys):
     out = capsys.readouterr().out.splitlines()
     assert out[0].startswith("[bench] Model: 1L x 128d, 2H/2KVH, dtype=float32, runtime_mode=archived")
     assert out[1].startswith("prefill(len=8): mean=") and out[2].startswith("decode(steps=5): mean=")
+
+
+def _run_bench(args, env_extra=None):
+    import json
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parent.parent
+    env = dict(os.environ, **(env_extra or {}))
+    proc = subprocess.run([sys.executable, str(root / "bench.py"), *args], cwd=root, env=env, capture_output=True,
+                          text=True, timeout=300)
+    assert proc.returncode == 0, proc.stderr[-2000:]
+    lines = [ln for ln in proc.stdout.splitlines() if ln.startswith("{")]
+    return [json.loads(ln) for ln in lines]
+
+
+def test_reference_arm_prints_one_contract_line_on_host_cores():
+    """bench.py --impl reference: the reference algorithm on the host cores,
+    one JSON line with the arm's metric, a cpu_baseline describing the run and
+    an e2e object without device copies."""
+    (line,) = _run_bench(["--impl", "reference", "--workload", "decode8k_fp16", "--steps", "1", "--warmup", "0"])
+    assert line["impl"] == "reference" and line["n_gpus"] == 1 and line["steps"] == 1
+    assert line["unit"] == "tokens/s" and line["higher_is_better"] is True and line["value"] > 0
+    assert line["config"]["workload"] == "decode8k_fp16"
+    cpu = line["cpu_baseline"]
+    assert cpu["kind"] in ("port", "reference") and cpu["cores"] >= 1 and cpu["value"] == line["value"]
+    assert line["e2e"] == {"value": line["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+
+
+def test_reference_arm_runs_on_rank_zero_only():
+    assert _run_bench(["--impl", "reference", "--workload", "decode8k_fp16", "--steps", "1", "--warmup", "0"],
+                      {"RANK": "1", "LOCAL_RANK": "1", "WORLD_SIZE": "2"}) == []
