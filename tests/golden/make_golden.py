@@ -325,14 +325,17 @@ def make_tiny_model(mx, out_path: Path) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("RFSN_REFERENCE", "/root/reference"))
+    ap.add_argument("--out", default=str(HERE), help="directory the fixtures are written to")
     args = ap.parse_args()
+    out = Path(args.out).resolve()
+    out.mkdir(parents=True, exist_ok=True)
     mx = _setup(Path(args.reference))
     os.chdir(tempfile.mkdtemp())
-    make_attention(mx, HERE / "segattn_golden.npz")
-    make_ring_traces(mx, HERE / "ring_traces.json")
-    make_residency_trace(mx, HERE / "residency_trace.json")
-    make_tiny_model(mx, HERE / "tiny_model_golden.npz")
-    for p in sorted(HERE.iterdir()):
+    make_attention(mx, out / "segattn_golden.npz")
+    make_ring_traces(mx, out / "ring_traces.json")
+    make_residency_trace(mx, out / "residency_trace.json")
+    make_tiny_model(mx, out / "tiny_model_golden.npz")
+    for p in sorted(out.iterdir()):
         if p.suffix in (".npz", ".json"):
             print(f"{p.name}: {p.stat().st_size} bytes")
 
