@@ -89,7 +89,7 @@ def _run(world, mode):
     return got
 
 
-@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("world", [2, 3, 4])
 def test_sharded_gather_and_merge_equals_unsharded(world):
     got = _run(world, "ok")
     for rank in range(world):
