@@ -257,7 +257,11 @@ RFSN_API rfsn_status rfsn_event_wait(void* event, int64_t timeout_us);
  * (attention_exact.py:111-164). Semantics: scaled dot products
  * (scale 1/sqrt(head_dim)), causal by absolute position (key pos <= query
  * pos, attention_exact.py:27-61), one softmax over every segment, float32
- * accumulation. Query head h reads KV head h / (q_heads / kv_heads).
+ * accumulation. Query head h reads KV head h / (q_heads / kv_heads). A query
+ * row that sees no key at all (every key after it) gets zeros and LSE -inf;
+ * the reference's additive -1e9 mask gives such a row the softmax of the
+ * masked scores instead. Decode and prefill never produce such a row: a
+ * query always sees its own key.
  *
  * q: device float32 [batch][q_heads][q_len][head_dim]; query row r sits at
  * absolute position q_pos0 + r. out: device float32, same shape. lse
