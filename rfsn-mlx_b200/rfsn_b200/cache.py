@@ -37,6 +37,7 @@ import shutil
 import time
 import uuid
 from collections.abc import Sequence
+from concurrent.futures import Future, ThreadPoolExecutor
 from pathlib import Path
 from typing import Any, Optional
 
@@ -291,7 +292,10 @@ class LayerKVCache:
         pool_tokens: Optional[int] = None,
         ops: Optional[Any] = None,
         host_tier: bool = False,
+        persist_async: bool = False,
     ) -> None:
+        if persist_async and not host_tier:
+            raise ValueError("persist_async requires host_tier=True (the pinned copy serves reloads meanwhile)")
         self.config = config
         self.batch_size = batch_size
         self.num_heads = num_heads
@@ -324,6 +328,16 @@ class LayerKVCache:
         # streams the block from pinned host memory on the side stream instead of
         # reading, verifying and decompressing the npz file.
         self._host_tier: Optional[dict[BlockId, tuple[torch.Tensor, torch.Tensor]]] = {} if host_tier else None
+        # Write-behind persistence (optional, host tier only): a demotion stages
+        # the manifest change on the caller's thread and one writer thread per
+        # layer compresses, hashes and writes the npz and sidecars in the order
+        # they were staged. flush_persistence() waits for them; restore and
+        # reset flush (or drop) them first.
+        self._writer: Optional[ThreadPoolExecutor] = (
+            ThreadPoolExecutor(max_workers=1, thread_name_prefix="rfsn-persist") if persist_async else None
+        )
+        self._write_jobs: list[Future] = []
+        self._persisted: set[BlockId] = set()
         self._deferred_free: list[tuple[int, int]] = []
         self._block_serial = 0
 
@@ -409,8 +423,44 @@ class LayerKVCache:
         self._attended, self._attended_spans = [], []
         self._dirty = True
 
+    def flush_persistence(self) -> None:
+        """Wait for every npz and sidecar write staged by write-behind demotions
+        of this layer; raises RuntimeError with the first failure."""
+        jobs, self._write_jobs = self._write_jobs, []
+        first: Optional[BaseException] = None
+        for job in jobs:
+            try:
+                job.result()
+            except Exception as exc:  # noqa: BLE001 - reported below, after every job has ended
+                first = first or exc
+        if first is not None:
+            raise RuntimeError(f"write-behind persistence failed at layer {self.layer_id}: {first}") from first
+
+    def _drop_pending_writes(self) -> None:
+        """Cancel staged writes that have not started and wait for the running one."""
+        jobs, self._write_jobs = self._write_jobs, []
+        for job in jobs:
+            job.cancel()
+        for job in jobs:
+            if not job.cancelled():
+                try:
+                    job.result()
+                except Exception:  # noqa: BLE001 - the files are being removed anyway
+                    pass
+        self._persisted.clear()
+
+    def _stage_write(self, fn, *args) -> None:
+        self._write_jobs = [j for j in self._write_jobs if not j.done() or j.exception() is not None]
+        self._write_jobs.append(self._writer.submit(fn, *args))
+
     def reset(self, *, clear_persisted: bool = True) -> None:
         """cache.py:137-150."""
+        if self._writer is not None:
+            if clear_persisted:
+                self._drop_pending_writes()
+            else:
+                self.flush_persistence()
+                self._persisted.clear()
         self._clear_device_state()
         self.hot_seq_len = 0
         self.hot_start = 0
@@ -425,6 +475,9 @@ class LayerKVCache:
 
     def restore_from_disk(self) -> list[BlockManifest]:
         """cache.py:152-175: rebuild the page table from persisted manifests."""
+        if self._writer is not None:
+            self.flush_persistence()
+            self._persisted.clear()
         self._clear_device_state()
         self.hot_seq_len = 0
         self.hot_head_index = 0
@@ -530,8 +583,11 @@ class LayerKVCache:
             return
         if self._host_tier is not None:
             n = manifest.token_count
-            if manifest.block_id in self._host_tier and manifest.checksum and manifest.payload_path \
-                    and Path(manifest.payload_path).exists():
+            if self._writer is not None:
+                persisted = manifest.block_id in self._persisted
+            else:
+                persisted = bool(manifest.checksum and manifest.payload_path and Path(manifest.payload_path).exists())
+            if manifest.block_id in self._host_tier and persisted:
                 # already persisted and held in pinned memory: the state change of
                 # persist_block without rewriting identical bytes
                 self._free_rows(row, n)
@@ -539,17 +595,30 @@ class LayerKVCache:
                 manifest.materializable = True
                 manifest.failure_reason = None
                 manifest.touch()
-                self.storage.write_manifest(manifest)
+                if self._writer is not None:
+                    self._stage_write(self.storage.write_snapshot, manifest, manifest.to_dict())
+                else:
+                    self.storage.write_manifest(manifest)
                 return
             k_pin, v_pin = self._ops.download_pinned(row, n)
             self._free_rows(row, n)
             self._host_tier[manifest.block_id] = (k_pin, v_pin)
             out = np.float16 if self.storage_array_dtype == np.float16 else np.float32
             shape = (self.batch_size, self.num_kv_heads, n, self.config.head_dim)
-            payload = {"keys": k_pin.to(torch.float32).numpy().astype(out).reshape(shape),
-                       "values": v_pin.to(torch.float32).numpy().astype(out).reshape(shape)}
-            manifest.dtype = payload["keys"].dtype.name
-            self.storage.persist_block(manifest, payload)
+
+            def payload() -> dict[str, np.ndarray]:
+                return {"keys": k_pin.to(torch.float32).numpy().astype(out).reshape(shape),
+                        "values": v_pin.to(torch.float32).numpy().astype(out).reshape(shape)}
+
+            if self._writer is not None:
+                self.storage.stage_persist(manifest, np.dtype(out).name)
+                self._persisted.add(manifest.block_id)
+                snapshot = manifest.to_dict()
+                self._stage_write(lambda: self.storage.write_staged(manifest, snapshot, payload()))
+                return
+            arrays = payload()
+            manifest.dtype = arrays["keys"].dtype.name
+            self.storage.persist_block(manifest, arrays)
             return
         payload = self._download_block(row, manifest.token_count)
         self._free_rows(row, manifest.token_count)
@@ -934,6 +1003,7 @@ class RFSNCache:
         pool_tokens: Optional[int] = None,
         ops_factory: Optional[Any] = None,
         host_tier: bool = False,
+        persist_async: bool = False,
     ) -> None:
         self.config = config
         self.model_id = model_id or derive_model_id(config)
@@ -951,9 +1021,15 @@ class RFSNCache:
                 pool_tokens=pool_tokens,
                 ops=ops_factory() if ops_factory is not None else None,
                 host_tier=host_tier,
+                persist_async=persist_async,
             )
             for i in range(config.num_layers)
         ]
+
+    def flush_persistence(self) -> None:
+        """Wait for every layer's write-behind npz and sidecar writes."""
+        for layer_cache in self.layers:
+            layer_cache.flush_persistence()
 
     @property
     def model_root(self) -> Path:
@@ -979,6 +1055,7 @@ class RFSNCache:
             f"Restore requested for session '{self.session_id}' but no persisted archive exists "
             f"for model '{self.model_id}'"
         )
+        self.flush_persistence()  # writes staged by this object land before the archive is read
         if not self.model_root.exists():
             raise FileNotFoundError(missing)
         if not self.session_root.exists():

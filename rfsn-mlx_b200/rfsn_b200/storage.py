@@ -113,6 +113,44 @@ class BlockStorage:
             raise
         return manifest
 
+    # -- write-behind (a cache that holds demoted blocks in pinned host memory) ----------
+    def stage_persist(self, manifest: BlockManifest, dtype_name: str) -> None:
+        """The in-memory effect of persist_block, without the bytes: payload and
+        sidecar paths, dtype, COLD_DISK, materializable, the access stamp. The
+        checksum stays empty until write_staged has hashed the payload."""
+        if manifest.payload_format != "npz":
+            raise ValueError(f"Unsupported payload_format '{manifest.payload_format}'")
+        payload_path, sidecar = self._paths(manifest)
+        manifest.payload_path = str(payload_path)
+        manifest.manifest_path = str(sidecar)
+        manifest.dtype = dtype_name
+        manifest.checksum = ""
+        manifest.residency = BlockLocation.COLD_DISK
+        manifest.materializable = True
+        manifest.failure_reason = None
+        manifest.touch()
+
+    def write_staged(self, manifest: BlockManifest, snapshot: dict[str, Any], payload: Mapping[str, np.ndarray]) -> str:
+        """Writer side of stage_persist: the compressed payload, its SHA-256 (set
+        on the manifest) and the sidecar as staged, with that checksum."""
+        arrays = {name: np.asarray(arr) for name, arr in payload.items()}
+        buffer = io.BytesIO()
+        np.savez_compressed(buffer, **arrays)
+        blob = buffer.getvalue()
+        checksum = hashlib.sha256(blob).hexdigest()
+        _atomic_write(Path(snapshot["payload_path"]), blob)
+        manifest.checksum = checksum
+        self.write_snapshot(manifest, snapshot)
+        return checksum
+
+    def write_snapshot(self, manifest: BlockManifest, snapshot: dict[str, Any]) -> None:
+        """Writer side of a sidecar update staged as ``manifest.to_dict()``; a
+        checksum the snapshot lacks comes from the payload write staged before it."""
+        if not snapshot.get("checksum") and manifest.checksum:
+            snapshot = dict(snapshot, checksum=manifest.checksum)
+        _atomic_write(Path(snapshot["manifest_path"]),
+                      json.dumps(snapshot, indent=2, sort_keys=True).encode("utf-8"))
+
     def write_manifest(self, manifest: BlockManifest) -> BlockManifest:
         _, sidecar = self._paths(manifest)
         manifest.manifest_path = str(sidecar)

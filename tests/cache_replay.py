@@ -77,13 +77,15 @@ def replay_ring(name, ops_factory):
         return cache
 
 
-def replay_residency(name, ops_factory, host_tier=False):
+def replay_residency(name, ops_factory, host_tier=False, persist_async=False, at_end=None):
+    """``at_end(cache, cfg)`` runs after the last step, while the session files still exist."""
     from rfsn_b200 import LayerKVCache
 
     sc = RESIDENCY[name]
     with tempfile.TemporaryDirectory() as tmp:
         cfg = _config(sc["hot_capacity"], sc["block_size"], "archived", sc["warm_capacity"], tmp)
-        cache = LayerKVCache(cfg, 1, 2, 1, layer_id=0, session_id="golden", ops=ops_factory(), host_tier=host_tier)
+        cache = LayerKVCache(cfg, 1, 2, 1, layer_id=0, session_id="golden", ops=ops_factory(), host_tier=host_tier,
+                             persist_async=persist_async)
         pos = 0
         for step in sc["steps"]:
             n = step["incoming"]
@@ -104,6 +106,8 @@ def replay_residency(name, ops_factory, host_tier=False):
             assert [float(s[0][0, 0, 0, 0]) for s in segs] == step["segment_first_values"]
             assert cache.residency_manager.get_metrics() == step["metrics"]
             assert [cache.hot_head_index, cache.hot_seq_len, cache.hot_start] == step["hot"]
+        if at_end is not None:
+            at_end(cache, cfg)
         return cache
 
 

@@ -247,3 +247,88 @@ def test_random_append_sequences_match_ring_oracle(seed):
                 expect = torch.arange(start, start + kk.shape[2], dtype=torch.float32)
                 assert torch.equal(kk[0, 0, :, 0].float().cpu(), expect)
                 assert torch.equal(vv[0, 0, :, 0].float().cpu(), expect + 0.5)
+
+
+def _check_persisted_session(cache, cfg):
+    """After a flush every cold block's npz and sidecar are on disk, the
+    sidecar's checksum is the SHA-256 of the npz, the payload is the block's
+    rows, and a fresh cache restores the same page table from the files."""
+    import hashlib
+
+    from rfsn_b200 import LayerKVCache
+
+    cache.flush_persistence()
+    cold = [m for m in cache.block_manager.iter_blocks(layer_id=0) if m.residency == BlockLocation.COLD_DISK]
+    assert cold, "the trace demotes blocks"
+    for m in cold:
+        blob = Path(m.payload_path).read_bytes()
+        assert m.checksum == hashlib.sha256(blob).hexdigest()
+        side = json.loads(Path(m.manifest_path).read_text())
+        assert side["checksum"] == m.checksum and side["residency"] == "cold_disk"
+        loaded = cache.storage.load_block(m)
+        pos = np.arange(m.logical_start, m.logical_end, dtype=np.float32)
+        np.testing.assert_array_equal(loaded["keys"][0, 0, :, 0], pos)
+        np.testing.assert_array_equal(loaded["values"][0, 0, :, 0], -pos)
+    spans = [(m.logical_start, m.logical_end) for m in cache.block_manager.iter_blocks(layer_id=0)]
+    fresh = LayerKVCache(cfg, 1, 2, 1, layer_id=0, session_id="golden", ops=FakeDeviceOps())
+    restored = fresh.restore_from_disk()
+    assert [(m.logical_start, m.logical_end) for m in restored] == spans
+
+
+@pytest.mark.parametrize("name", residency_names())
+def test_write_behind_persistence_keeps_reference_decisions(name):
+    # npz writes on the layer's writer thread: residency decisions, metrics and
+    # attended values equal the reference trace, and the files written after a
+    # flush restore the session
+    replay_residency(name, FakeDeviceOps, host_tier=True, persist_async=True, at_end=_check_persisted_session)
+
+
+def test_write_behind_needs_the_host_tier(tmp_path):
+    from cache_replay import _config
+    from rfsn_b200 import LayerKVCache
+
+    with pytest.raises(ValueError, match="host_tier"):
+        LayerKVCache(_config(8, 4, "archived", 8, str(tmp_path)), 1, 2, 1, session_id="s", ops=FakeDeviceOps(),
+                     persist_async=True)
+
+
+def test_write_behind_reset_drops_pending_writes_and_reports_failures(tmp_path, monkeypatch):
+    import threading
+
+    import torch
+
+    from cache_replay import _config, _kv
+    from rfsn_b200 import LayerKVCache
+
+    cfg = _config(4, 4, "archived", 4, str(tmp_path))
+    cache = LayerKVCache(cfg, 1, 2, 1, session_id="s", ops=FakeDeviceOps(), host_tier=True, persist_async=True)
+    gate = threading.Event()
+    real = cache.storage.write_staged
+
+    def slow(*a, **kw):
+        gate.wait(timeout=10)
+        return real(*a, **kw)
+
+    monkeypatch.setattr(cache.storage, "write_staged", slow)
+    pos = 0
+    for _ in range(6):  # hot 4, blocks of 4, warm 4 tokens: every append seals, older blocks go cold
+        cache.evict_for_append(4)
+        k, v = _kv(pos, 4, torch.device("cpu"))
+        cache.append_exact(k, v)
+        pos += 4
+    assert cache._write_jobs and not any(j.done() for j in cache._write_jobs)
+    gate.set()
+    cache.reset(clear_persisted=True)
+    assert cache._write_jobs == [] and not list(cache.storage.root_dir.glob("*.npz"))
+
+    def broken(*a, **kw):
+        raise OSError("disk full")
+
+    monkeypatch.setattr(cache.storage, "write_staged", broken)
+    for _ in range(4):
+        cache.evict_for_append(4)
+        k, v = _kv(pos, 4, torch.device("cpu"))
+        cache.append_exact(k, v)
+        pos += 4
+    with pytest.raises(RuntimeError, match="disk full"):
+        cache.flush_persistence()
