@@ -111,6 +111,39 @@ def replay_residency(name, ops_factory, host_tier=False, persist_async=False, at
         return cache
 
 
+def check_persisted_session(ops_factory):
+    """``at_end`` check for a write-behind replay: after a flush every cold
+    block's npz and sidecar are on disk, the sidecar's checksum is the SHA-256
+    of the npz, the payload holds the block's rows, and a fresh cache restores
+    the same page table from the files."""
+
+    def check(cache, cfg):
+        import hashlib
+        import json
+        from pathlib import Path
+
+        from rfsn_b200 import LayerKVCache
+        from rfsn_b200.block_manager import BlockLocation
+
+        cache.flush_persistence()
+        cold = [m for m in cache.block_manager.iter_blocks(layer_id=0) if m.residency == BlockLocation.COLD_DISK]
+        assert cold, "the trace demotes blocks"
+        for m in cold:
+            blob = Path(m.payload_path).read_bytes()
+            assert m.checksum == hashlib.sha256(blob).hexdigest()
+            side = json.loads(Path(m.manifest_path).read_text())
+            assert side["checksum"] == m.checksum and side["residency"] == "cold_disk"
+            loaded = cache.storage.load_block(m)
+            pos = torch.arange(m.logical_start, m.logical_end, dtype=torch.float32).numpy()
+            assert (loaded["keys"][0, 0, :, 0] == pos).all() and (loaded["values"][0, 0, :, 0] == -pos).all()
+        spans = [(m.logical_start, m.logical_end) for m in cache.block_manager.iter_blocks(layer_id=0)]
+        fresh = LayerKVCache(cfg, 1, 2, 1, layer_id=0, session_id="golden", ops=ops_factory())
+        restored = fresh.restore_from_disk()
+        assert [(m.logical_start, m.logical_end) for m in restored] == spans
+
+    return check
+
+
 def ring_names():
     return sorted(RING)
 

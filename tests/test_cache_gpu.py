@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 import torch
 
-from cache_replay import replay_residency, replay_ring, residency_names, ring_names
+from cache_replay import check_persisted_session, replay_residency, replay_ring, residency_names, ring_names
 from oracle.rope import apply_rope, inv_freq, rope_tables
 from oracle.segmented_attention import run_segmented_attention
 
@@ -25,6 +25,14 @@ def test_ring_trace_on_device(name):
 @pytest.mark.parametrize("name", residency_names())
 def test_residency_trace_on_device(name, host_tier):
     replay_residency(name, lambda: None, host_tier=host_tier)
+
+
+@pytest.mark.parametrize("name", residency_names())
+def test_residency_trace_on_device_with_write_behind(name):
+    # demotions download into pinned memory and return; the npz writes land on
+    # the layer's writer thread and restore the session after a flush
+    replay_residency(name, lambda: None, host_tier=True, persist_async=True,
+                     at_end=check_persisted_session(lambda: None))
 
 
 def _round(x, dtype):

@@ -8,7 +8,7 @@ from pathlib import Path
 import numpy as np
 import pytest
 
-from cache_replay import replay_residency, replay_ring, residency_names, ring_names
+from cache_replay import check_persisted_session, replay_residency, replay_ring, residency_names, ring_names
 from fake_ops import FakeDeviceOps
 from rfsn_b200 import (
     BlockId,
@@ -249,38 +249,13 @@ def test_random_append_sequences_match_ring_oracle(seed):
                 assert torch.equal(vv[0, 0, :, 0].float().cpu(), expect + 0.5)
 
 
-def _check_persisted_session(cache, cfg):
-    """After a flush every cold block's npz and sidecar are on disk, the
-    sidecar's checksum is the SHA-256 of the npz, the payload is the block's
-    rows, and a fresh cache restores the same page table from the files."""
-    import hashlib
-
-    from rfsn_b200 import LayerKVCache
-
-    cache.flush_persistence()
-    cold = [m for m in cache.block_manager.iter_blocks(layer_id=0) if m.residency == BlockLocation.COLD_DISK]
-    assert cold, "the trace demotes blocks"
-    for m in cold:
-        blob = Path(m.payload_path).read_bytes()
-        assert m.checksum == hashlib.sha256(blob).hexdigest()
-        side = json.loads(Path(m.manifest_path).read_text())
-        assert side["checksum"] == m.checksum and side["residency"] == "cold_disk"
-        loaded = cache.storage.load_block(m)
-        pos = np.arange(m.logical_start, m.logical_end, dtype=np.float32)
-        np.testing.assert_array_equal(loaded["keys"][0, 0, :, 0], pos)
-        np.testing.assert_array_equal(loaded["values"][0, 0, :, 0], -pos)
-    spans = [(m.logical_start, m.logical_end) for m in cache.block_manager.iter_blocks(layer_id=0)]
-    fresh = LayerKVCache(cfg, 1, 2, 1, layer_id=0, session_id="golden", ops=FakeDeviceOps())
-    restored = fresh.restore_from_disk()
-    assert [(m.logical_start, m.logical_end) for m in restored] == spans
-
-
 @pytest.mark.parametrize("name", residency_names())
 def test_write_behind_persistence_keeps_reference_decisions(name):
     # npz writes on the layer's writer thread: residency decisions, metrics and
     # attended values equal the reference trace, and the files written after a
     # flush restore the session
-    replay_residency(name, FakeDeviceOps, host_tier=True, persist_async=True, at_end=_check_persisted_session)
+    replay_residency(name, FakeDeviceOps, host_tier=True, persist_async=True,
+                     at_end=check_persisted_session(FakeDeviceOps))
 
 
 def test_write_behind_needs_the_host_tier(tmp_path):
