@@ -31,6 +31,12 @@ arm alone.
 At N = 1 the line also carries ``secondary`` (the 8K fp16 decode workload)
 and ``prefill``: one layer of a 32K-token prompt prefilled in 2048-token
 chunks on the tcgen05 tensor-core kernel, against the measured bf16 peak.
+
+Other workloads (one GPU, one JSON line each): ``prefill32k_chunk2048_bf16``,
+``warm_reload_bf16`` (decode steps that reload cold blocks), and the whole
+models ``model8b_e2e_bf16`` (Llama-3-8B shape) and
+``model7b_prefill32k_warm_bf16`` (Mistral-7B shape, 32K prompt, half the
+archived blocks in the pinned host tier; ``--decode-steps N``, default 128).
 """
 
 from __future__ import annotations
@@ -847,6 +853,96 @@ def run_model(args):
     return 0
 
 
+MODEL7B_WORKLOAD = "model7b_prefill32k_warm_bf16"
+MODEL7B_DESC = ("Mistral-7B-shaped model, random init normal(0, 0.02) seed 5: 32 layers, hidden 4096, 32 q / 8 kv "
+                "heads, head_dim 128, SwiGLU FFN 14336, vocab 32000, RoPE theta 1e6, bf16; 32,768-token prompt of "
+                "uniform random ids prefilled in chunks of 2,048 (tensor-core chunk attention over every archived "
+                "block), then greedy decode steps; hot ring 4,096, block size 512, warm capacity 14,336 tokens per "
+                "layer, so half the archived blocks are cold, held in pinned host memory and reloaded by every "
+                "decode step (the reference's residency policy); npz persistence of demotions write-behind")
+
+
+def run_model7b(args):
+    """``--workload model7b_prefill32k_warm_bf16``: whole-model chunked prefill of a
+    32K prompt and greedy decode with half of every layer's archived blocks in the
+    pinned host tier (demotions persisted write-behind). A throwaway 2,048-token
+    prefill and two decode steps on a separate cache warm up cuBLAS and the
+    kernels; the timed run starts from an empty cache. Decode runs op by op (the
+    cold blocks change the page table every step)."""
+    import torch
+
+    from rfsn_b200.cache import RFSNCache
+    from rfsn_b200.config import RFSNConfig, RuntimeMode
+    from rfsn_b200.model import RFSNModel
+
+    if args.impl == "reference":
+        print(json.dumps({"impl": "reference", "unavailable": "the 7B-shaped model needs a GPU; the reference CPU "
+                          "arm times the decode-attention workloads"}), flush=True)
+        return 0
+    torch.cuda.set_device(0)
+    device = torch.device("cuda", 0)
+    prompt_len, chunk = 32768, 2048
+    n_decode = args.decode_steps if args.decode_steps is not None else 128
+    with tempfile.TemporaryDirectory() as tmp:
+        cfg = RFSNConfig(hidden_dim=4096, num_heads=32, num_kv_heads=8, head_dim=128, num_layers=32,
+                         vocab_size=32000, ffn_dim=14336, rope_base=1e6, norm_eps=1e-5, model_dtype="bfloat16",
+                         hot_capacity=4096, block_size_seq=512, warm_capacity=14336, cold_capacity=65536,
+                         runtime_mode=RuntimeMode.ARCHIVED, disk_cache_dir=tmp, session_id="bench7b")
+        model = RFSNModel(cfg, device=device, seed=5)
+        gen = torch.Generator().manual_seed(5)
+        prompt = torch.randint(0, cfg.vocab_size, (1, prompt_len), generator=gen, dtype=torch.int32)
+
+        warm = RFSNCache(cfg, batch_size=1, device=device, host_tier=True, persist_async=True,
+                         session_id="bench7b_warmup")
+        logits = model.prefill(prompt[:, :chunk], warm)
+        tok = torch.argmax(logits[:, -1, :], dim=-1).to(torch.int32)
+        for pos in range(chunk, chunk + 2):
+            tok = torch.argmax(model.decode_step(tok, warm, pos), dim=-1).to(torch.int32)
+        torch.cuda.synchronize()
+        warm.reset()
+        del warm, logits
+
+        cache = RFSNCache(cfg, batch_size=1, device=device, host_tier=True, persist_async=True)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        ev[0].record()
+        for a in range(0, prompt_len, chunk):
+            logits = model.prefill(prompt[:, a:a + chunk], cache)
+        ev[1].record()
+        tok = torch.argmax(logits[:, -1, :], dim=-1).to(torch.int32)
+        for pos in range(prompt_len, prompt_len + n_decode):
+            tok = torch.argmax(model.decode_step(tok, cache, pos), dim=-1).to(torch.int32)
+        ev[2].record()
+        ev[2].synchronize()
+        pre_ms, dec_ms = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
+        layer0 = cache.layer(0)
+        blocks = list(layer0.block_manager.iter_blocks(layer_id=0))
+        cold = sum(1 for m in blocks if not layer0.is_manifest_resident(m))
+        metrics: dict = {}
+        for lc in cache.layers:
+            for k, v in lc.residency_manager.get_metrics().items():
+                metrics[k] = metrics.get(k, 0) + v
+        pending = sum(1 for lc in cache.layers for j in lc._write_jobs if not j.done())
+        cache.reset()  # drops the npz writes still queued (the session is not kept)
+    pairs = prompt_len * (prompt_len + 1) // 2
+    line = {
+        "metric": "model end-to-end chunked prefill tokens/s and decode tokens/s with warm-tier reloads "
+                  "(Mistral-7B shape, bf16)",
+        "workload": MODEL7B_WORKLOAD, "desc": MODEL7B_DESC, "n_gpus": 1, "dtype": "bf16",
+        "data": "synthetic: random weights and prompt ids (seeded)", "higher_is_better": True,
+        "value": prompt_len / (pre_ms / 1e3), "unit": "prefill tokens/s", "prefill_ms": pre_ms,
+        "prefill_attention_tflop": 4 * cfg.num_heads * cfg.head_dim * pairs * cfg.num_layers / 1e12,
+        "decode_steps": n_decode, "decode_ms_per_token": dec_ms / max(n_decode, 1),
+        "decode_tokens_per_s": n_decode / (dec_ms / 1e3) if n_decode else None,
+        "layer0_blocks_after": len(blocks), "layer0_cold_blocks_after": cold,
+        "residency_metrics_all_layers": metrics, "npz_writes_pending_at_end": pending,
+        "notes": "prefill projections and the LM head on cuBLAS; RMSNorm, SwiGLU, RoPE+append, seals, the tcgen05 "
+                 "chunk attention and the paged decode attention on this library's kernels; cold blocks reload from "
+                 "pinned host memory on the side stream; npz persistence on a writer thread per layer",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_prefill(args):
     """``--workload prefill32k_chunk2048_bf16``: the chunked-prefill measurement as
     its own line (1 GPU; the reference arm has no GPU counterpart)."""
@@ -871,11 +967,13 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + [PREFILL_WORKLOAD, MODEL_WORKLOAD, WARM_WORKLOAD], default="decode128k_bf16")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + [PREFILL_WORKLOAD, MODEL_WORKLOAD, WARM_WORKLOAD, MODEL7B_WORKLOAD], default="decode128k_bf16")
     ap.add_argument("--calls-per-step", type=int, default=200)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the chunked-prefill measurement (N = 1)")
+    ap.add_argument("--decode-steps", type=int, default=None,
+                    help="greedy decode steps of the model7b workload (default 128)")
     ap.add_argument("--merge", choices=["p2p", "nccl"], default="p2p",
                     help="cross-GPU merge for N > 1: fused NVLink mailboxes (default) or NCCL all-gather")
     args = ap.parse_args()
@@ -887,6 +985,8 @@ def main() -> int:
         return run_model(args)
     if args.workload == WARM_WORKLOAD:
         return run_warm(args)
+    if args.workload == MODEL7B_WORKLOAD:
+        return run_model7b(args)
     w = WORKLOADS[args.workload]
     if args.impl == "reference":
         return run_reference(args, w)
