@@ -34,6 +34,7 @@ from __future__ import annotations
 import hashlib
 import json
 import shutil
+import threading
 import time
 import uuid
 from collections.abc import Sequence
@@ -338,6 +339,10 @@ class LayerKVCache:
         )
         self._write_jobs: list[Future] = []
         self._persisted: set[BlockId] = set()
+        # Sidecar rewrites not yet started, one per block: a newer state of the
+        # same block replaces the queued one instead of queueing another write.
+        self._queued_sidecars: dict[BlockId, dict[str, Any]] = {}
+        self._sidecar_lock = threading.Lock()
         self._deferred_free: list[tuple[int, int]] = []
         self._block_serial = 0
 
@@ -448,10 +453,26 @@ class LayerKVCache:
                 except Exception:  # noqa: BLE001 - the files are being removed anyway
                     pass
         self._persisted.clear()
+        with self._sidecar_lock:
+            self._queued_sidecars.clear()
 
     def _stage_write(self, fn, *args) -> None:
         self._write_jobs = [j for j in self._write_jobs if not j.done() or j.exception() is not None]
         self._write_jobs.append(self._writer.submit(fn, *args))
+
+    def _stage_sidecar(self, manifest: BlockManifest) -> None:
+        snapshot = manifest.to_dict()
+        with self._sidecar_lock:
+            queued = manifest.block_id in self._queued_sidecars
+            self._queued_sidecars[manifest.block_id] = snapshot
+        if not queued:
+            self._stage_write(self._write_queued_sidecar, manifest)
+
+    def _write_queued_sidecar(self, manifest: BlockManifest) -> None:
+        with self._sidecar_lock:
+            snapshot = self._queued_sidecars.pop(manifest.block_id, None)
+        if snapshot is not None:
+            self.storage.write_snapshot(manifest, snapshot)
 
     def reset(self, *, clear_persisted: bool = True) -> None:
         """cache.py:137-150."""
@@ -596,7 +617,7 @@ class LayerKVCache:
                 manifest.failure_reason = None
                 manifest.touch()
                 if self._writer is not None:
-                    self._stage_write(self.storage.write_snapshot, manifest, manifest.to_dict())
+                    self._stage_sidecar(manifest)
                 else:
                     self.storage.write_manifest(manifest)
                 return

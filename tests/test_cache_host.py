@@ -307,3 +307,44 @@ def test_write_behind_reset_drops_pending_writes_and_reports_failures(tmp_path, 
         pos += 4
     with pytest.raises(RuntimeError, match="disk full"):
         cache.flush_persistence()
+
+
+def test_write_behind_coalesces_sidecar_rewrites(tmp_path, monkeypatch):
+    """Thrashing blocks between warm and cold queues at most one sidecar write
+    per block while the writer is busy; after a flush each cold block's sidecar
+    is its current manifest, as a synchronous write would have left it."""
+    import threading
+
+    import torch
+
+    from cache_replay import _config, _kv
+    from rfsn_b200 import LayerKVCache
+
+    cfg = _config(4, 4, "archived", 8, str(tmp_path))
+    cache = LayerKVCache(cfg, 1, 2, 1, session_id="s", ops=FakeDeviceOps(), host_tier=True, persist_async=True)
+    pos = 0
+    for _ in range(6):  # 5 sealed blocks of 4 tokens, 2 of them warm
+        cache.evict_for_append(4)
+        k, v = _kv(pos, 4, torch.device("cpu"))
+        cache.append_exact(k, v)
+        pos += 4
+    cache.flush_persistence()
+    gate = threading.Event()
+    real = cache.storage.write_snapshot
+
+    def held(*a, **kw):
+        gate.wait(timeout=10)
+        return real(*a, **kw)
+
+    monkeypatch.setattr(cache.storage, "write_snapshot", held)
+    blocks = list(cache.block_manager.iter_blocks(layer_id=0))
+    for _ in range(20):  # every call reloads the cold blocks and demotes others (the reference's thrash)
+        cache.get_attention_segments()
+    evictions = cache.residency_manager.get_metrics()["warm_evictions"]
+    # at most: the running write, one first-time payload write and one queued sidecar per block
+    assert len(cache._write_jobs) <= 2 * len(blocks) + 1 < evictions
+    gate.set()
+    cache.flush_persistence()
+    for m in cache.block_manager.iter_blocks(layer_id=0):
+        if m.residency == BlockLocation.COLD_DISK:
+            assert json.loads(Path(m.manifest_path).read_text()) == m.to_dict()
