@@ -19,6 +19,7 @@ import logging
 import os
 import tempfile
 import time
+import zipfile
 from collections.abc import Mapping
 from pathlib import Path
 from typing import Any, Optional
@@ -59,6 +60,23 @@ def _atomic_write(target: Path, data: bytes) -> None:
             tmp.unlink(missing_ok=True)
 
 
+# Deflate level of the npz payloads. The layout is numpy's savez_compressed
+# (one ``<name>.npy`` member per array, deflate, zip64), so np.load and the
+# reference read these files unchanged; level 1 compresses a 2,048-token block
+# about 7x faster than numpy's default level for a file about 10 % larger.
+NPZ_DEFLATE_LEVEL = 1
+
+
+def _npz_bytes(arrays: Mapping[str, np.ndarray]) -> bytes:
+    buffer = io.BytesIO()
+    with zipfile.ZipFile(buffer, mode="w", compression=zipfile.ZIP_DEFLATED,
+                         compresslevel=NPZ_DEFLATE_LEVEL) as archive:
+        for name, arr in arrays.items():
+            with archive.open(f"{name}.npy", mode="w", force_zip64=True) as member:
+                np.lib.format.write_array(member, np.asanyarray(arr), allow_pickle=False)
+    return buffer.getvalue()
+
+
 def _safe_fragment(value: str) -> str:
     return "".join(c if (c.isalnum() or c in "-_") else "_" for c in value)
 
@@ -93,9 +111,7 @@ class BlockStorage:
         arrays = self._normalize(payload, manifest)
         if manifest.payload_format != "npz":
             raise ValueError(f"Unsupported payload_format '{manifest.payload_format}'")
-        buffer = io.BytesIO()
-        np.savez_compressed(buffer, **arrays)
-        blob = buffer.getvalue()
+        blob = _npz_bytes(arrays)
         payload_path, sidecar = self._paths(manifest)
         manifest.payload_path = str(payload_path)
         manifest.manifest_path = str(sidecar)
@@ -134,9 +150,7 @@ class BlockStorage:
         """Writer side of stage_persist: the compressed payload, its SHA-256 (set
         on the manifest) and the sidecar as staged, with that checksum."""
         arrays = {name: np.asarray(arr) for name, arr in payload.items()}
-        buffer = io.BytesIO()
-        np.savez_compressed(buffer, **arrays)
-        blob = buffer.getvalue()
+        blob = _npz_bytes(arrays)
         checksum = hashlib.sha256(blob).hexdigest()
         _atomic_write(Path(snapshot["payload_path"]), blob)
         manifest.checksum = checksum
