@@ -348,3 +348,25 @@ def test_write_behind_coalesces_sidecar_rewrites(tmp_path, monkeypatch):
     for m in cache.block_manager.iter_blocks(layer_id=0):
         if m.residency == BlockLocation.COLD_DISK:
             assert json.loads(Path(m.manifest_path).read_text()) == m.to_dict()
+
+
+def test_npz_payload_layout_matches_numpy_savez():
+    """Payloads are numpy's npz layout at a faster deflate level: the same
+    member names and arrays as np.savez_compressed, read back by np.load."""
+    import io
+    import zipfile
+
+    from rfsn_b200.storage import NPZ_DEFLATE_LEVEL, _npz_bytes
+
+    arrays = {"keys": np.arange(2 * 3 * 5 * 4, dtype=np.float32).reshape(2, 3, 5, 4),
+              "values": -np.ones((2, 3, 5, 4), np.float16)}
+    ours = _npz_bytes(arrays)
+    ref = io.BytesIO()
+    np.savez_compressed(ref, **arrays)
+    names = lambda blob: sorted(i.filename for i in zipfile.ZipFile(io.BytesIO(blob)).infolist())  # noqa: E731
+    assert names(ours) == names(ref.getvalue()) == ["keys.npy", "values.npy"]
+    assert all(i.compress_type == zipfile.ZIP_DEFLATED for i in zipfile.ZipFile(io.BytesIO(ours)).infolist())
+    assert NPZ_DEFLATE_LEVEL == 1
+    loaded = np.load(io.BytesIO(ours))
+    for k, v in arrays.items():
+        assert loaded[k].dtype == v.dtype and np.array_equal(loaded[k], v)
