@@ -152,6 +152,14 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------------------------ setup
+def _extra(fn):
+    """Result of an optional part of the JSON line, or {"error": ...} if it raised."""
+    try:
+        return fn()
+    except Exception as exc:  # noqa: BLE001 - reported in the line
+        return {"error": f"{type(exc).__name__}: {exc}"}
+
+
 def dist_env():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -460,18 +468,23 @@ def run_ours(args, w):
     prefill = None
     cpu = None
     if world == 1 and rank == 0:
+        # The headline is measured by now: a failing extra is reported in the
+        # line instead of taking the line with it.
         if args.workload == "decode128k_bf16" and not args.no_secondary:
-            secondary = secondary_8k(args, device, peak)
+            secondary = _extra(lambda: secondary_8k(args, device, peak))
         if not args.no_prefill:
-            prefill = prefill_32k(args, device)
+            prefill = _extra(lambda: prefill_32k(args, device))
         if not args.no_cpu_baseline:
-            sec, n, threads = cpu_baseline_sample(w)
-            cpu = {
-                "value": 1.0 / sec, "unit": "tokens/s", "cores": threads, "kind": "port",
-                "sample": f"median of {n} full decode-attention calls over the {total_tokens}-token context after 1 "
-                          "warm-up; the reference algorithm (float32 upcast, GQA repeat, two passes) restated in "
-                          "numpy, KV heads on a thread pool",
-            }
+            def cpu_line():
+                sec, n, threads = cpu_baseline_sample(w)
+                return {
+                    "value": 1.0 / sec, "unit": "tokens/s", "cores": threads, "kind": "port",
+                    "sample": f"median of {n} full decode-attention calls over the {total_tokens}-token context "
+                              "after 1 warm-up; the reference algorithm (float32 upcast, GQA repeat, two passes) "
+                              "restated in numpy, KV heads on a thread pool",
+                }
+
+            cpu = _extra(cpu_line)
 
     if rank == 0:
         line = {
