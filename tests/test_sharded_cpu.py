@@ -123,3 +123,31 @@ def test_shard_ranges_partition_blocks_contiguously():
             ranges = [shard_range(n, r, world) for r in range(world)]
             assert ranges[0][0] == 0 and ranges[-1][1] == n
             assert all(a[1] == b[0] for a, b in zip(ranges, ranges[1:]))
+
+
+def test_balanced_shards_random_layouts():
+    """Random block lists and hot windows: ranges are contiguous and cover every
+    block, and each rank's end boundary is the block boundary closest to its
+    share of the tokens among the boundaries not before the previous rank's."""
+    hyp = pytest.importorskip("hypothesis")
+    st = hyp.strategies
+    from rfsn_b200.sharded import balanced_shards
+
+    @hyp.settings(max_examples=300, deadline=None, derandomize=True)
+    @hyp.given(blocks=st.lists(st.integers(1, 4096), min_size=0, max_size=200), hot=st.integers(0, 8192),
+               world=st.sampled_from([1, 2, 3, 4, 8]))
+    def check(blocks, hot, world):
+        ranges = balanced_shards(blocks, hot, world)
+        assert len(ranges) == world and ranges[0][0] == 0 and ranges[-1][1] == len(blocks)
+        assert all(lo <= hi for lo, hi in ranges) and all(a[1] == b[0] for a, b in zip(ranges, ranges[1:]))
+        cum = [0]
+        for n in blocks:
+            cum.append(cum[-1] + n)
+        total = cum[-1] + hot
+        for r in range(1, world):
+            target = total * r / world
+            b = ranges[r][0]
+            allowed = range(ranges[r - 1][0], len(blocks) + 1)
+            assert all(abs(cum[b] - target) <= abs(cum[x] - target) for x in allowed)
+
+    check()
