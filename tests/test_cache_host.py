@@ -370,3 +370,42 @@ def test_npz_payload_layout_matches_numpy_savez():
     loaded = np.load(io.BytesIO(ours))
     for k, v in arrays.items():
         assert loaded[k].dtype == v.dtype and np.array_equal(loaded[k], v)
+
+
+def test_session_restore_errors_and_round_trip_match_reference(tmp_path):
+    """cache.py:488-559: restoring needs an explicit session id, a missing
+    archive and an unknown session raise FileNotFoundError (the latter listing
+    the sessions that exist), and a persisted session restores its page table."""
+    import dataclasses
+
+    import torch
+
+    from cache_replay import _config, _kv
+    from rfsn_b200 import RFSNCache
+
+    base = _config(4, 4, "archived", 4, str(tmp_path))
+    alpha, beta = dataclasses.replace(base, session_id="alpha"), dataclasses.replace(base, session_id="beta")
+    with pytest.raises(ValueError, match="explicit session_id"):
+        RFSNCache(base, 1, restore=True, ops_factory=FakeDeviceOps)
+    with pytest.raises(FileNotFoundError, match="no persisted archive exists"):
+        RFSNCache(alpha, 1, restore=True, ops_factory=FakeDeviceOps).restore_from_disk()
+
+    kv = RFSNCache(alpha, 1, ops_factory=FakeDeviceOps)
+    layer = kv.layer(0)
+    pos = 0
+    for _ in range(5):  # blocks of 4 beyond a warm capacity of 4 tokens go to disk
+        layer.evict_for_append(4)
+        k, v = _kv(pos, 4, torch.device("cpu"))
+        layer.append_exact(k, v)
+        pos += 4
+    # restore rebuilds the persisted (cold) blocks; a block still warm was never written
+    spans = [(m.logical_start, m.logical_end) for m in layer.block_manager.iter_blocks(layer_id=0)
+             if m.residency == BlockLocation.COLD_DISK]
+    assert len(spans) >= 2
+
+    with pytest.raises(FileNotFoundError, match="unknown session 'beta'.*Available sessions: alpha"):
+        RFSNCache(beta, 1, restore=True, ops_factory=FakeDeviceOps).restore_from_disk()
+    restored = RFSNCache(alpha, 1, restore=True, ops_factory=FakeDeviceOps)
+    (manifests,) = restored.restore_from_disk()
+    assert [(m.logical_start, m.logical_end) for m in manifests] == spans
+    assert restored.layer(0).hot_start == spans[-1][1]
