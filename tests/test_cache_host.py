@@ -409,3 +409,19 @@ def test_session_restore_errors_and_round_trip_match_reference(tmp_path):
     (manifests,) = restored.restore_from_disk()
     assert [(m.logical_start, m.logical_end) for m in manifests] == spans
     assert restored.layer(0).hot_start == spans[-1][1]
+
+
+@pytest.mark.parametrize("head_dim,base", [(64, 10000.0), (128, 500000.0), (128, 1e6)])
+def test_rope_frequency_table_matches_oracle_on_host(tmp_path, head_dim, base):
+    # layer.py:29 in float32; the table the fused RoPE kernel reads
+    import dataclasses
+
+    from cache_replay import _config
+    from oracle.rope import inv_freq
+    from rfsn_b200 import LayerKVCache
+
+    cfg = dataclasses.replace(_config(8, 4, "archived", 8, str(tmp_path)), head_dim=head_dim, rope_base=base,
+                              hidden_dim=2 * head_dim)
+    c = LayerKVCache(cfg, 1, 2, 1, session_id="r", ops=FakeDeviceOps())
+    table = c.inv_freq().numpy()
+    assert table.dtype == np.float32 and np.array_equal(table, inv_freq(head_dim, base))
