@@ -343,9 +343,12 @@ RFSN_API rfsn_status rfsn_lse_merge(const float* parts_out, const float* parts_l
  * the process exits. Calls sharing a device share the array; calls that
  * overlap on the GPU race and must be ordered by the caller. Shapes whose
  * split scratch does not fit are rejected with RFSN_ERR_OVERFLOW (lower
- * max_splits, or use rfsn_paged_attention). The first call on each device
- * looks up the array's device address (cudaGetSymbolAddress) and should be
- * made before any stream capture.
+ * max_splits, or use rfsn_paged_attention); a rejected call issues no CUDA
+ * work. The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress) and should be made before any stream capture.
+ * Kernel-side failures (an expired bounded wait, a page-table record outside
+ * the arena) set the array's error word, which stays set until
+ * rfsn_noalloc_check reads it.
  * ---------------------------------------------------------------------- */
 #define RFSN_NOALLOC_SCRATCH_BYTES (8u << 20)
 
@@ -356,6 +359,13 @@ RFSN_API rfsn_status rfsn_paged_attention_noalloc(const rfsn_arena* arena,
                                          const rfsn_hot_window* hot,
                                          float* out, float* lse,
                                          int max_splits, void* stream);
+
+/* Error check of rfsn_paged_attention_noalloc on the current device (no
+ * counterpart in the reference): waits for `stream` (bounded by timeout_us),
+ * then reads and clears the built-in array's error word, with the statuses of
+ * rfsn_workspace_check (RFSN_ERR_TIMEOUT for an expired wait, RFSN_ERR_DEVICE
+ * for a record outside the arena). Allocates no device memory. */
+RFSN_API rfsn_status rfsn_noalloc_check(void* stream, int64_t timeout_us);
 
 /* Number of kernels this library has launched in the process so far
  * (instrumentation: lets callers count native launches in a timed region). */
@@ -371,7 +381,11 @@ RFSN_API uint64_t rfsn_launch_count(void);
  * all ranks in rank order (the merge of attention_exact.py:141-164), so every
  * rank ends with the full result after one kernel, without a collective
  * library call. Waits for peers are bounded (rfsn_peer_group_set_timeout,
- * default 2 s) and report RFSN_ERR_DEVICE through rfsn_workspace_check.
+ * default 2 s) and report RFSN_ERR_TIMEOUT through rfsn_workspace_check.
+ * After a peer wait has expired the group is unusable: its later calls skip
+ * the exchange, write this rank's local result and report RFSN_ERR_TIMEOUT
+ * again (the ranks' call stamps no longer agree), until every rank destroys
+ * the group and creates a new one.
  *
  * Set-up per rank: rfsn_peer_group_create (allocates the mailbox on the
  * current device and writes its CUDA IPC handle, rfsn_peer_ipc_handle_bytes()

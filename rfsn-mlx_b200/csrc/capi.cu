@@ -582,7 +582,7 @@ rfsn_status rfsn_paged_attention(const rfsn_arena* arena, const float* q, int ba
 rfsn_status rfsn::paged_attention_impl(const rfsn_arena* arena, const float* q, int batch, int q_heads, int kv_heads,
                                        int q_len, int q_pos0, const rfsn_page_table* table, const rfsn_hot_window* hot,
                                        float* out, float* lse, void* workspace, size_t workspace_bytes, int max_splits,
-                                       const PeerParams* peer, cudaStream_t s) {
+                                       const PeerParams* peer, cudaStream_t s, bool dry_run) {
     RFSN_CHECK_ARG(arena != nullptr && table != nullptr && hot != nullptr, "rfsn_paged_attention: NULL arena/table/hot");
     CommonArgs a;
     rfsn_status st = check_common(q, batch, q_heads, kv_heads, q_len, arena->head_dim, out, workspace, &a);
@@ -659,6 +659,7 @@ rfsn_status rfsn::paged_attention_impl(const rfsn_arena* arena, const float* q, 
         pp.groups_per_kv = a.G;
         pp.qscale = qscale_for(128);
         pp.ws = ws_view(workspace, w);
+        if (dry_run) return RFSN_OK;
         return prefill_launch(arena->dtype, arena->maps, pp, s);
     }
     if (peer != nullptr && !use_fast) {
@@ -708,6 +709,7 @@ rfsn_status rfsn::paged_attention_impl(const rfsn_arena* arena, const float* q, 
         memset(&p.peer, 0, sizeof(p.peer));
         if (peer != nullptr) p.peer = *peer;
         p.dyn = hot->step_state;
+        if (dry_run) return RFSN_OK;
         return fast_launch(arena->dtype, arena->maps, p, kFastStages, s);
     }
     generic::Params p;
@@ -749,6 +751,7 @@ rfsn_status rfsn::paged_attention_impl(const rfsn_arena* arena, const float* q, 
     p.head = hot->head_index;
     p.hlen = hot->length;
     p.hstart = hot->start_pos;
+    if (dry_run) return RFSN_OK;
     return generic_launch(arena->dtype, true, p, a.groups, s);
 }
 
@@ -826,7 +829,8 @@ rfsn_status rfsn_workspace_check(void* workspace, void* stream, int64_t timeout_
         const int zero = 0;
         RFSN_CUDA(cudaMemcpy(workspace, &zero, sizeof(int), cudaMemcpyHostToDevice));
         if (word == kDevErrPeerTimeout) {
-            set_error("attention kernel: the cross-GPU merge timed out waiting for a peer's partial results");
+            set_error("attention kernel: the cross-GPU merge timed out waiting for a peer's partial results (in this "
+                      "call or an earlier one of the same peer group; the group must be destroyed and created again)");
             return RFSN_ERR_TIMEOUT;
         }
         if (word == kDevErrTimeout) {

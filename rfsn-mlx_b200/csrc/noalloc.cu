@@ -11,10 +11,17 @@
 //
 // The array is kNoallocScratchBytes long and every GPU that loads this library
 // holds its own copy until the process exits. All calls on a device share it
-// and it keeps whatever the previous call left there; the counters that must
-// start at zero are cleared (cudaMemsetAsync, no allocation) at the start of
-// every call. Calls whose execution overlaps on the GPU (different streams, or
-// different host threads) race on the array and must be ordered by the caller.
+// and it keeps whatever the previous call left there; the arrival counters
+// that must start at zero are cleared (cudaMemsetAsync, no allocation) at the
+// start of every accepted call. Calls whose execution overlaps on the GPU
+// (different streams, or different host threads) race on the array and must be
+// ordered by the caller.
+//
+// Kernel-side failures (a bounded wait that expired, a page-table record
+// outside the arena) are recorded in the array's error word, which no call
+// clears: rfsn_noalloc_check reads it (after the stream's work is done) and
+// resets it, like rfsn_workspace_check does for a caller's workspace. An
+// error therefore stays visible until it is checked.
 //
 // The device address of the array is looked up with cudaGetSymbolAddress the
 // first time the entry point runs on each device, with that device current.
@@ -23,7 +30,7 @@
 #include <mutex>
 #include <string>
 
-#include "common.cuh"
+#include "params.cuh"
 
 namespace {
 
@@ -64,19 +71,18 @@ extern "C" rfsn_status rfsn_paged_attention_noalloc(const rfsn_arena* arena, con
                                                     int kv_heads, int q_len, int q_pos0, const rfsn_page_table* table,
                                                     const rfsn_hot_window* hot, float* out, float* lse, int max_splits,
                                                     void* stream) {
-    // Pointer arguments are rejected before the set-up and the counter clear,
-    // so a bad call issues no CUDA work at all.
     RFSN_CHECK_ARG(arena != nullptr && table != nullptr && hot != nullptr,
                    "rfsn_paged_attention_noalloc: NULL arena/table/hot");
     RFSN_CHECK_ARG(q != nullptr && out != nullptr, "rfsn_paged_attention_noalloc: NULL q/out");
     void* scratch = nullptr;
     rfsn_status st = scratch_address(&scratch);
     if (st != RFSN_OK) return st;
-    // Error word and arrival counters must start at zero.
-    RFSN_CUDA(cudaMemsetAsync(scratch, 0, 256 + sizeof(int) * (size_t)rfsn::kMaxCounters,
-                              static_cast<cudaStream_t>(stream)));
-    st = rfsn_paged_attention(arena, q, batch, q_heads, kv_heads, q_len, q_pos0, table, hot, out, lse, scratch,
-                              kNoallocScratchBytes, max_splits, stream);
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // Every check of the real call first (shape, page table, hot window, the
+    // scratch size the chosen kernel needs), without launching: a rejected call
+    // issues no CUDA work and leaves the shared array as it was.
+    st = rfsn::paged_attention_impl(arena, q, batch, q_heads, kv_heads, q_len, q_pos0, table, hot, out, lse, scratch,
+                                    kNoallocScratchBytes, max_splits, nullptr, s, /*dry_run=*/true);
     if (st == RFSN_ERR_OVERFLOW) {
         // The shape needs more split scratch than the built-in array holds.
         const std::string inner = rfsn_last_error();
@@ -85,5 +91,17 @@ extern "C" rfsn_status rfsn_paged_attention_noalloc(const rfsn_arena* arena, con
             "a smaller max_splits or use rfsn_paged_attention with a caller-provided workspace",
             kNoallocScratchBytes, inner.c_str());
     }
-    return st;
+    if (st != RFSN_OK) return st;
+    // The arrival counters must start at zero; the error word (offset 0) is left
+    // for rfsn_noalloc_check.
+    RFSN_CUDA(cudaMemsetAsync(static_cast<char*>(scratch) + 256, 0, sizeof(int) * (size_t)rfsn::kMaxCounters, s));
+    return rfsn::paged_attention_impl(arena, q, batch, q_heads, kv_heads, q_len, q_pos0, table, hot, out, lse, scratch,
+                                      kNoallocScratchBytes, max_splits, nullptr, s);
+}
+
+extern "C" rfsn_status rfsn_noalloc_check(void* stream, int64_t timeout_us) {
+    void* scratch = nullptr;
+    rfsn_status st = scratch_address(&scratch);
+    if (st != RFSN_OK) return st;
+    return rfsn_workspace_check(scratch, stream, timeout_us);
 }

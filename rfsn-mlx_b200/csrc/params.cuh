@@ -85,7 +85,9 @@ rfsn_status generic_launch(int dtype, bool paged, const generic::Params& p, int 
 rfsn_status paged_attention_impl(const rfsn_arena* arena, const float* q, int batch, int q_heads, int kv_heads,
                                  int q_len, int q_pos0, const rfsn_page_table* table, const rfsn_hot_window* hot,
                                  float* out, float* lse, void* workspace, size_t workspace_bytes, int max_splits,
-                                 const PeerParams* peer, cudaStream_t stream);
+                                 const PeerParams* peer, cudaStream_t stream, bool dry_run = false);
+// dry_run: every argument check, the kernel choice and the workspace sizing of
+// a real call, then return without launching (status as the call would give).
 // prefill_attn.cu
 rfsn_status prefill_launch(int dtype, const CUtensorMap* maps, const PrefillParams& p, cudaStream_t stream);
 // merge.cu

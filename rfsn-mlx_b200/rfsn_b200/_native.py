@@ -58,6 +58,7 @@ EXPORTED_SYMBOLS = (
     "rfsn_workspace_check",
     "rfsn_launch_count",
     "rfsn_paged_attention_noalloc",
+    "rfsn_noalloc_check",
     "rfsn_peer_ipc_handle_bytes",
     "rfsn_peer_group_create",
     "rfsn_peer_group_connect",
@@ -181,6 +182,7 @@ def load_library() -> ctypes.CDLL:
             i32,
             [vp, vp, i32, i32, i32, i32, i32, ctypes.POINTER(PageTableC), ctypes.POINTER(HotWindowC), vp, vp, i32, vp],
         ),
+        "rfsn_noalloc_check": (i32, [vp, i64]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
