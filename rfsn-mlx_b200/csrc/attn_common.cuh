@@ -157,6 +157,15 @@ __host__ __device__ constexpr int merge_scratch_floats(int nslots, int splits) {
 __device__ __forceinline__ void peer_store_and_merge(const PeerParams& peer, const WsView& ws, int call, int group,
                                                      int sl, int d4, int head_dim, float4 r, float my_lse,
                                                      const OutMap& om, float* out, float* lse) {
+    if (*reinterpret_cast<volatile const int*>(peer.poison) != 0) {
+        // An earlier call of this group gave up waiting for a peer: the ranks'
+        // call stamps may no longer agree, so words carrying this call's stamp
+        // could belong to another decode step. Keep the local result and fail.
+        *reinterpret_cast<float4*>(out + om.row(group, sl) * head_dim + 4 * d4) = r;
+        if (lse != nullptr && d4 == 0) lse[om.row(group, sl)] = my_lse;
+        if (d4 == 0) atomicExch(ws.error, kDevErrPeerTimeout);
+        return;
+    }
     const int P = peer.world;
     const int groups = (int)gridDim.y;  // grid = splits x groups
     const size_t slot_words = (size_t)head_dim + 2;
@@ -229,7 +238,10 @@ __device__ __forceinline__ void peer_store_and_merge(const PeerParams& peer, con
             }
         }
     }
-    if (timed_out) atomicExch(ws.error, kDevErrPeerTimeout);
+    if (timed_out) {
+        atomicExch(peer.poison, 1);
+        atomicExch(ws.error, kDevErrPeerTimeout);
+    }
     const float inv = W > 0.f ? 1.f / W : 0.f;
     *reinterpret_cast<float4*>(out + om.row(group, sl) * head_dim + 4 * d4) =
         make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);

@@ -262,6 +262,9 @@ constexpr int kDevErrBadTable = 2;  // a page-table record points outside the ar
 
 // Cross-GPU exchange of the fused sharded merge (see peer.cu). Each rank owns
 // a mailbox in its HBM that every peer maps with CUDA IPC:
+//   poison int32            set once a wait for a peer has expired (local only):
+//                           the ranks' call stamps may then disagree, so later
+//                           calls skip the exchange and report the timeout again
 //   calls  int32 [groups]   this rank's call counter per group (local only)
 //   words  uint2 [2][kMaxPeers][groups][kPeerSlots][head_dim + 2]
 //          (call parity, source rank, group, query slot; head_dim output
@@ -279,6 +282,7 @@ struct PeerParams {
     int rank;
     uint2* words[kMaxPeers];       // every rank's word region (own one included)
     int* calls;                    // own call counters
+    int* poison;                   // own group-state word: non-zero once a peer wait has expired
     long long timeout_ns;          // bounded wait for peers
 };
 

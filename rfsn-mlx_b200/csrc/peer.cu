@@ -123,6 +123,7 @@ rfsn_status rfsn_paged_attention_peer(const rfsn_arena* arena, const float* q, i
         pp.words[r] = reinterpret_cast<uint2*>(base + peers->words_off);
     }
     pp.calls = reinterpret_cast<int*>(static_cast<char*>(peers->local) + peers->calls_off);
+    pp.poison = static_cast<int*>(peers->local);  // header word 0 of the own mailbox
     pp.timeout_ns = peers->timeout_ns;
     return rfsn::paged_attention_impl(arena, q, batch, q_heads, kv_heads, q_len, q_pos0, table, hot, out, lse, workspace,
                                       workspace_bytes, max_splits, &pp, static_cast<cudaStream_t>(stream));

@@ -248,6 +248,15 @@ def _silent_peer_worker(rank, port, results):
                 torch.cuda.synchronize()
                 ws.check()
                 msg += f" | finite={bool(torch.isfinite(out).all())}"
+                # the group is unusable now: a second peer call does not wait, does not
+                # merge words left from the expired call, and reports the timeout again
+                again = paged_attention(cache, qd, total - 1, segs, peers=peers)
+                try:
+                    ws.check(timeout_s=30.0)
+                    msg += " | second call: no error"
+                except TimeoutError:
+                    msg += " | second call: timeout"
+                msg += f" | second call local={bool(torch.equal(again, out))}"
             dist.barrier()  # rank 1 stays idle until rank 0 is done
             peers.close()
             results.put((rank, msg))
@@ -267,7 +276,8 @@ def test_peer_merge_timeout_is_reported_and_context_survives():
     for p in procs:
         p.join(timeout=120)
     assert got[0].startswith("timeout:") and "the cross-GPU merge timed out" in got[0], got[0]
-    assert got[0].endswith("finite=True"), got[0]
+    assert "finite=True" in got[0], got[0]
+    assert got[0].endswith("second call: timeout | second call local=True"), got[0]
     assert got[1] == "no call", got[1]
 
 
