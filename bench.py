@@ -227,6 +227,119 @@ def max_over_ranks(x: float, world: int) -> float:
     return float(t.item())
 
 
+PARITY_TOL = 2e-3  # max-abs bar for attention outputs (fp16/bf16 K/V, float32 accumulation)
+
+
+def _parity_q(w, device):
+    """The query of the parity calls: the same seeded tensor on every rank."""
+    import torch
+
+    gen = torch.Generator(device=device).manual_seed(w["seed"] * 7919 + 17)
+    return torch.randn((1, w["q_heads"], 1, w["head_dim"]), generator=gen, device=device, dtype=torch.float32)
+
+
+def _dense_context(w, device):
+    """The whole context's K/V in logical order, regenerated from the per-block
+    seeds ``build_shard`` uses (archived blocks, then the hot ring), float64."""
+    import torch
+
+    dt = {"bfloat16": torch.bfloat16, "float16": torch.float16}[w["dtype"]]
+    ks, vs = [], []
+    gen = torch.Generator(device=device)
+    for i, n in enumerate(w["blocks"]):
+        gen.manual_seed(w["seed"] * 100003 + i)
+        shape = (w["kv_heads"], n, w["head_dim"])
+        ks.append(torch.randn(shape, generator=gen, device=device, dtype=torch.float32).to(dt).double())
+        vs.append(torch.randn(shape, generator=gen, device=device, dtype=torch.float32).to(dt).double())
+    gen.manual_seed(w["seed"] * 100003 + 99991)
+    shape = (w["kv_heads"], w["hot"], w["head_dim"])
+    ks.append(torch.randn(shape, generator=gen, device=device, dtype=torch.float32).to(dt).double())
+    vs.append(torch.randn(shape, generator=gen, device=device, dtype=torch.float32).to(dt).double())
+    return torch.cat(ks, dim=1), torch.cat(vs, dim=1)
+
+
+def _dense_attention(q, k, v):
+    """softmax(q k^T / sqrt(D)) v over every key (the query is the last token),
+    query head h on KV head h // G; float64."""
+    import torch
+
+    Hq, D = q.shape[1], q.shape[3]
+    G = Hq // k.shape[0]
+    qh = q[0, :, 0, :].double().view(k.shape[0], G, D)                   # [Hkv, G, D]
+    p = (torch.bmm(qh, k.transpose(1, 2)) / (D ** 0.5)).softmax(dim=-1)  # [Hkv, G, T]
+    return torch.bmm(p, v).reshape(1, Hq, 1, D)                          # [1, Hq, 1, D]
+
+
+E2E_EXTRA = [0]  # extra ring tokens a full-context replay cache must hold (set by run_ours)
+
+
+def static_parity(cache, w, world, rank, device, total_tokens, peers):
+    """Correctness of the timed call: every rank makes one more call of the
+    timed kind (local attention + the cross-GPU merge at N > 1) with a fixed
+    query; rank 0 compares the merged output with (a) the single-GPU kernel
+    over the whole context (rank 0 rebuilds it from the per-block seeds; at
+    N = 1 that is the timed kernel itself, so only (b) is reported) and (b) a
+    dense float64 softmax over the same keys. Returns (rank 0) the figures and
+    a fresh full-context cache for the end-to-end check."""
+    import torch
+
+    from rfsn_b200.cache import paged_attention
+    from rfsn_b200.sharded import merge_across_ranks
+
+    q = _parity_q(w, device)
+    pos = total_tokens - 1
+    segs = cache.get_attention_segments()
+    if world > 1 and peers is not None:
+        got = paged_attention(cache, q, pos, segs, peers=peers)
+    elif world > 1:
+        if len(segs) == 0:
+            out = torch.zeros_like(q)
+            lse = torch.full(q.shape[:3], float("-inf"), device=device)
+        else:
+            out, lse = paged_attention(cache, q, pos, segs, want_lse=True)
+        got = merge_across_ranks(out, lse)
+    else:
+        got = paged_attention(cache, q, pos, segs)
+    torch.cuda.synchronize()
+    res = None
+    if rank == 0:
+        def figures():
+            r = {}
+            full = build_shard(w, 0, 1, device, E2E_EXTRA[0])[0]
+            if world > 1:
+                ref1 = paged_attention(full, q, pos, full.get_attention_segments())
+                r["max_abs_vs_1gpu"] = float((got - ref1).abs().max())
+            k64, v64 = _dense_context(w, device)
+            dense = _dense_attention(q, k64, v64)
+            del k64, v64
+            r["max_abs_vs_dense_fp64"] = float((got.double() - dense).abs().max())
+            r["query_position"] = pos
+            return r, full
+        try:
+            res = figures()
+        except Exception as exc:  # noqa: BLE001 - reported in the line
+            res = ({"error": f"{type(exc).__name__}: {exc}"}, None)
+    barrier(world)
+    return res
+
+
+def e2e_parity(full, w, e2e_info):
+    """Rank 0: the last output of the end-to-end loop against the same token
+    sequence replayed through ``attention_step`` (op by op, public API) on the
+    single-GPU full-context cache."""
+    import torch
+
+    from rfsn_b200.layer import attention_step
+
+    pos0, n_calls, q_h, k_h, v_h, last = e2e_info
+    q, k, v = (t.to(full.device) for t in (q_h, k_h, v_h))
+    out = None
+    for i in range(n_calls):
+        out = attention_step(q, k, v, full, pos0 + i)
+    torch.cuda.synchronize()
+    return {"max_abs_vs_1gpu_replay": float((out.cpu() - last).abs().max()), "calls_replayed": n_calls}
+
+
 # ------------------------------------------------------------------------------------ measurements
 def device_throughput(cache, w, world, steps, warmup, calls_per_step, *, collective: bool, peers=None):
     """calls/s with inputs resident: CUDA-graph-captured calls, CUDA events."""
@@ -349,7 +462,9 @@ def e2e_throughput(cache, w, world, owns_hot, steps, calls_per_step, peers=None)
     else:
         h2d = q_h.numel() * q_h.element_size() + (k_h.numel() * k_h.element_size() * 2 if owns_hot else 0)
     d2h = out_h.numel() * out_h.element_size()
-    return elapsed, n, launches, h2d, d2h
+    last = (graphed.out_host if graphed is not None else out_h).clone()
+    info = (pos - 3, n + 3, q_h, k_h, v_h, last)  # every call made, for a replay check
+    return elapsed, n, launches, h2d, d2h, info
 
 
 def cpu_baseline_sample(w, budget_s=20.0):
@@ -367,7 +482,7 @@ def run_reference(args, w):
     if rank != 0:
         return 0
     per_step = []
-    threads = os.cpu_count() or 1
+    threads = len(os.sched_getaffinity(0)) or os.cpu_count() or 1
     from oracle.cpu_baseline import attention_all_cores, synthetic_decode_inputs, time_calls
 
     q, segs, qpos = synthetic_decode_inputs(w["blocks"], w["hot"], w["kv_heads"], w["q_heads"], w["head_dim"],
@@ -398,7 +513,7 @@ def run_reference(args, w):
         "cpu_baseline": {
             "value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
             "sample": f"{args.steps} full decode-attention calls over the {tokens}-token context; the reference "
-                      "algorithm (float32 upcast, GQA repeat, two passes) restated in numpy, KV heads on a thread pool",
+                      "algorithm (float32 upcast, GQA repeat, two passes) restated in numpy, (KV head, segment run) items on a thread pool with one BLAS thread per worker",
         },
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -422,6 +537,7 @@ def run_ours(args, w):
     device = torch.device("cuda", torch.cuda.current_device())
     e2e_calls = max(1, min(args.calls_per_step, 50))
     extra = args.steps * e2e_calls + 8
+    E2E_EXTRA[0] = extra
     cache, owns_hot, local_tokens, total_tokens = build_shard(w, rank, world, device, extra)
     torch.cuda.synchronize()
 
@@ -440,6 +556,8 @@ def run_ours(args, w):
     clocks = sampler.stop()
     ms = max_over_ranks(ms, world)
     k_ms_max = max_over_ranks(k_ms, world)
+    # correctness of what was timed (outside the timed region)
+    static = static_parity(cache, w, world, rank, device, total_tokens, peers)
 
     calls = args.steps * args.calls_per_step
     value = calls / (ms / 1e3)
@@ -449,8 +567,21 @@ def run_ours(args, w):
     achieved = local_bytes / k_call_s / 1e9
 
     # e2e through the public API (appends the new token each call)
-    e_elapsed, e_n, e_launches, h2d, d2h = e2e_throughput(cache, w, world, owns_hot, args.steps, e2e_calls, peers)
+    e_elapsed, e_n, e_launches, h2d, d2h, e2e_info = e2e_throughput(cache, w, world, owns_hot, args.steps, e2e_calls,
+                                                                     peers)
     e_elapsed = max_over_ranks(e_elapsed, world)
+    parity = None
+    if rank == 0:
+        figs, full = static
+        parity = {"tol": PARITY_TOL, "timed_call": figs}
+        if full is not None:
+            parity["e2e_call"] = _extra(lambda: e2e_parity(full, w, e2e_info))
+        vals = [v for d in (parity["timed_call"], parity.get("e2e_call", {})) for k_, v in d.items()
+                if k_.startswith("max_abs")]
+        parity["ok"] = (bool(vals) and all(v <= PARITY_TOL for v in vals)
+                        and "error" not in parity["timed_call"] and "error" not in parity.get("e2e_call", {}))
+        del full
+    barrier(world)
 
     traffic = None
     prof = ROOT / "profiles" / f"{args.workload}_traffic.json"
@@ -459,10 +590,10 @@ def run_ours(args, w):
             traffic = json.loads(prof.read_text()).get("dram_bytes_per_launch")
         except Exception:
             traffic = None
-    if traffic is not None and world > 1:
-        # captured on the whole context on one GPU; a rank's launch reads its shard,
-        # and the traffic grows in proportion to the K/V bytes it walks
-        traffic = int(traffic * local_bytes / algorithmic_bytes(w, total_tokens))
+    if world > 1:
+        # the committed capture is of the whole context on one GPU; a shard's launch
+        # (which also runs the cross-GPU merge) has no capture of its own
+        traffic = None
 
     secondary = None
     prefill = None
@@ -481,7 +612,7 @@ def run_ours(args, w):
                     "value": 1.0 / sec, "unit": "tokens/s", "cores": threads, "kind": "port",
                     "sample": f"median of {n} full decode-attention calls over the {total_tokens}-token context "
                               "after 1 warm-up; the reference algorithm (float32 upcast, GQA repeat, two passes) "
-                              "restated in numpy, KV heads on a thread pool",
+                              "restated in numpy, (KV head, segment run) items on a thread pool with one BLAS thread per worker",
                 }
 
             cpu = _extra(cpu_line)
@@ -540,6 +671,7 @@ def run_ours(args, w):
             "gpu_launches": launches,
             "e2e_gpu_launches": e_launches,
             "clocks": clocks,
+            "parity": parity,
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
@@ -557,6 +689,9 @@ def run_ours(args, w):
         torch.cuda.synchronize()
         gc.collect()
         dist.destroy_process_group()
+    if rank == 0 and parity is not None and not parity["ok"]:
+        print(f"parity check failed (max-abs bar {PARITY_TOL}): {json.dumps(parity)}", file=sys.stderr, flush=True)
+        return 3
     return 0
 
 
@@ -680,6 +815,22 @@ def prefill_32k(args, device):
     end.synchronize()
     native.check(lib.rfsn_workspace_check(ws.data_ptr(), native.stream_ptr(), 30_000_000), "prefill workspace")
     ms = start.elapsed_time(end) / reps
+    # correctness of the last chunk (its output is what `out` holds now): the first
+    # and last query row of every (query block, KV head) unit against a dense
+    # float64 softmax over the keys in logical order (archived blocks, then the ring)
+    rows = sorted({r for qb in range(chunk // 32) for r in (32 * qb, 32 * qb + 31)})
+    q_pos0 = (n_chunks - 1) * chunk
+    keys_k = torch.cat([k[:, cap:cap + n_blocks_max * chunk], k[:, :cap]], dim=1).double()  # [Hkv, 32768, D]
+    keys_v = torch.cat([v[:, cap:cap + n_blocks_max * chunk], v[:, :cap]], dim=1).double()
+    qs = q[0][:, rows].double().view(Hkv, H // Hkv * len(rows), D)
+    sc = torch.bmm(qs, keys_k.transpose(1, 2)) / (D ** 0.5)                      # [Hkv, G * rows, 32768]
+    qpos = torch.tensor([q_pos0 + r for r in rows], device=device).repeat(H // Hkv)
+    sc.masked_fill_(torch.arange(keys_k.shape[1], device=device)[None, None, :] > qpos[None, :, None], float("-inf"))
+    dense = torch.bmm(sc.softmax(dim=-1), keys_v).view(1, H, len(rows), D)
+    parity = {"max_abs_vs_dense_fp64": float((out[:, :, rows].double() - dense).abs().max()),
+              "rows_checked": f"first and last row of every unit of the last chunk ({len(rows)} rows x {H} heads)",
+              "tol": PARITY_TOL}
+    del keys_k, keys_v, sc, dense
     arena.close()
     tflops = flops / (ms / 1e3) / 1e12
     peak, kind = bf16_peak()
@@ -701,6 +852,7 @@ def prefill_32k(args, device):
             "kernel": "rfsn::prefill::prefill_attn_kernel (tcgen05, TMEM accumulators)",
         },
         "l2": "K/V 67 MB + q/out per call; every chunk streams its whole causal context",
+        "parity": parity,
     }
 
 

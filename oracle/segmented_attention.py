@@ -50,6 +50,7 @@ def run_segmented_attention(
     *,
     return_lse: bool = False,
     grouped: bool = False,
+    q_positions=None,
 ):
     """attention_exact.py:122-164 (with the single-segment branch of :135-137).
 
@@ -61,11 +62,15 @@ def run_segmented_attention(
     ``grouped=True`` evaluates the same formula without materialising the GQA
     repeat (each KV head's query group is stacked along the query axis), which
     keeps 128K-token cases within memory.
+    ``q_positions`` (grouped evaluation) gives each query row its own absolute
+    position instead of ``q_start_pos + row``: sampled rows of a long chunk are
+    checked without evaluating every row. The mask rule is the same (key
+    position <= query position, build_causal_mask).
     """
     if not segments:
         raise RuntimeError("run_segmented_attention requires at least one KV segment")
-    if grouped:
-        return _grouped(q, segments, q_start_pos, return_lse)
+    if grouped or q_positions is not None:
+        return _grouped(q, segments, q_start_pos, return_lse, q_positions)
     q_f32 = np.asarray(q, dtype=np.float32)
     num_heads = q_f32.shape[1]
     scale = np.float32(1.0 / (q_f32.shape[-1] ** 0.5))
@@ -97,7 +102,7 @@ def run_segmented_attention(
     return out
 
 
-def _grouped(q: np.ndarray, segments: Sequence[Segment], q_start_pos: int, return_lse: bool):
+def _grouped(q: np.ndarray, segments: Sequence[Segment], q_start_pos: int, return_lse: bool, q_positions=None):
     q_f32 = np.asarray(q, dtype=np.float32)
     B, H, Lq, D = q_f32.shape
     Hkv = segments[0][0].shape[1]
@@ -109,7 +114,12 @@ def _grouped(q: np.ndarray, segments: Sequence[Segment], q_start_pos: int, retur
     for k, v, k_start in segments:
         k32 = np.asarray(k, dtype=np.float32)
         logits = np.matmul(qg, np.swapaxes(k32, -1, -2)) * scale
-        mask = build_causal_mask(Lq, k32.shape[2], q_start_pos, k_start)
+        if q_positions is None:
+            mask = build_causal_mask(Lq, k32.shape[2], q_start_pos, k_start)
+        else:
+            k_positions = np.arange(k_start, k_start + k32.shape[2])[None, :]
+            qp = np.asarray(q_positions, dtype=np.int64)[:, None]
+            mask = np.where(k_positions <= qp, 0.0, -1e9).astype(np.float32)[None, None]
         logits = logits + np.tile(mask, (1, 1, G, 1))
         local_max = logits.max(axis=-1, keepdims=True)
         global_max = local_max if global_max is None else np.maximum(global_max, local_max)

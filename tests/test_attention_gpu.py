@@ -216,6 +216,63 @@ def test_tensor_core_prefill_key_range_splits(dtype, q_len, blocks, hot):
     _check(lay, q, lay.total_tokens - q_len)
 
 
+def _prefill_32k_last_chunk(make_q, seed):
+    """The last 2,048-token chunk (positions 30,720-32,767) of a 32,768-token
+    prompt over 14 archived blocks of 2,048 plus the full 4,096-token ring,
+    32 q / 8 kv heads, bf16, under the launch plan that geometry gets (the
+    units of the partly filled last wave split over key ranges). Returns the
+    max-abs error of the first and last query row of every (query block, KV
+    head) unit, which include the chunk's first and last row, against the
+    oracle for all 32 heads (the LSE is checked too)."""
+    import ctypes
+
+    from rfsn_b200 import _native as native
+
+    q_pos0, chunk, archived = 30720, 2048, 14 * 2048
+    lay = make_layout("bfloat16", 1, 8, 128, [2048] * 14, 4096, 4096, 0, seed=seed, shuffle=False, gap=0)
+    assert lay.hot_start == archived and lay.total_tokens == q_pos0 + chunk
+    whole, splits, ctas = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    native.check(native.lib().rfsn_prefill_plan(1, 32, 8, chunk, q_pos0, archived, archived, 4096, ctypes.byref(whole),
+                                                ctypes.byref(splits), ctypes.byref(ctas)), "rfsn_prefill_plan")
+    assert splits.value > 1 and whole.value < 512, (whole.value, splits.value, ctas.value)
+    q = make_q(lay)
+    out, lse = run_paged(lay, q, q_pos0)
+    rows = sorted({r for qb in range(chunk // 32) for r in (32 * qb, 32 * qb + 31)})
+    ref, ref_lse = run_segmented_attention(q[:, :, rows], lay.oracle_segments(), q_pos0, return_lse=True, grouped=True,
+                                           q_positions=[q_pos0 + r for r in rows])
+    np.testing.assert_allclose(lse[:, :, rows], ref_lse, atol=1e-4, rtol=1e-5)
+    assert np.isfinite(out).all()
+    return float(np.abs(out[:, :, rows] - ref).max())
+
+
+def test_tensor_core_prefill_32k_prompt_last_chunk_sampled_rows():
+    """The chunk geometry of the 32K-prompt prefill workload with N(0, 1) data."""
+    err = _prefill_32k_last_chunk(lambda lay: _q(1085, 1, 32, 2048, 128), seed=85)
+    assert err <= ATOL and err <= GUARD, err
+
+
+def test_tensor_core_prefill_32k_prompt_last_chunk_with_an_attention_sink():
+    """The same chunk when one early key dominates every query's attention (an
+    attention sink at position 3): each query vector is the sink key of its KV
+    head, scaled, plus noise, so that key takes most of the probability mass.
+
+    The float32 tensor-core accumulator of P V then holds a value of the size
+    of that key's v row from the first tile on, and the small contributions of
+    the ~250 later 128-key tiles (16 MMAs each) are added to it; measured on
+    B200, the output error grows with the number of those accumulation steps,
+    to a few 1e-4 here, far above the ~4e-6 of N(0, 1) data but inside the
+    2e-3 bar. This pins that bound."""
+    from oracle.numerics import from_storage
+
+    def sink_q(lay):
+        k0 = from_storage(lay.k_store, lay.dtype)[:, lay.records[0, 0] + 3]  # [8, 128]: the key at position 3
+        noise = np.random.default_rng(86).standard_normal((1, 32, 2048, 128)).astype(np.float32)
+        return (np.repeat(k0, 4, axis=0)[None, :, None, :] * 1.5 + 0.3 * noise).astype(np.float32)
+
+    err = _prefill_32k_last_chunk(sink_q, seed=86)
+    assert err <= ATOL and err <= 1e-3, err
+
+
 @pytest.mark.parametrize("dtype,lens,cap,hot,head,G", [
     ("bfloat16", [300, 257, 64, 1000], 4096, 100, 4050, 4),   # short window in a large ring, wrapped: empty splits
     ("float16", [], 512, 500, 300, 4),                         # no archived block: every split starts in the ring

@@ -34,6 +34,21 @@ def test_oracle_lse_merge_equals_unsplit():
     np.testing.assert_allclose(merged, full, atol=2e-6)
 
 
+@pytest.mark.parametrize("case", CASES[:4], ids=[c["name"] for c in CASES[:4]])
+def test_oracle_rows_at_explicit_positions_equal_the_contiguous_chunk(case):
+    """Sampled query rows given with their own positions reproduce the same rows
+    of the contiguous evaluation (used to check long prefill chunks by sample)."""
+    segs = [(from_storage(k, case["dtype"]), from_storage(v, case["dtype"]), s) for k, v, s in case["segs"]]
+    q = case["q"]
+    Lq = q.shape[2]
+    full, full_lse = run_segmented_attention(q, segs, case["q_start"], return_lse=True)
+    rows = sorted({0, Lq - 1, Lq // 2})
+    part, part_lse = run_segmented_attention(q[:, :, rows], segs, case["q_start"], return_lse=True,
+                                             q_positions=[case["q_start"] + r for r in rows])
+    np.testing.assert_allclose(part, full[:, :, rows], atol=2e-6, rtol=0)
+    np.testing.assert_allclose(part_lse, full_lse[:, :, rows], atol=2e-6, rtol=1e-6)
+
+
 RING = load_json("ring_traces.json")
 
 
