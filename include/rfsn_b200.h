@@ -174,6 +174,24 @@ RFSN_API rfsn_status rfsn_rope_append_step(const void* q, const void* k, const v
                                            int head_dim, float* q_out, const rfsn_arena* arena, int ring_row0,
                                            int capacity, void* stream);
 
+/* RoPE from explicit cos/sin tables, fused with the append
+ * (layer.py:118-135 for a layer called with rope_tables, or without them,
+ * when the layer builds its tables in the model dtype, layer.py:118-126).
+ * cos_t / sin_t: device [len][head_dim] in tab_dtype, row l for position
+ * pos0 + l; both NULL to build them from inv_freq (float32 products and
+ * cos/sin, rounded to tab_dtype: build_rope_tables with dtype = tab_dtype).
+ * Every product and sum is rounded to the promoted dtype of in_dtype and
+ * tab_dtype (the 16-bit type when both are it, else float32), as the
+ * reference's elementwise ops round each result. q_out (float32) holds the
+ * rotated q; the rotated k and v go to ring slots write_index.. like
+ * rfsn_rope_append. */
+RFSN_API rfsn_status rfsn_rope_append_tables(const void* q, const void* k, const void* v, int in_dtype,
+                                             const void* cos_t, const void* sin_t, int tab_dtype,
+                                             const float* inv_freq, int pos0, int batch, int q_heads,
+                                             int kv_heads, int len, int head_dim, float* q_out,
+                                             const rfsn_arena* arena, int ring_row0, int capacity,
+                                             int write_index, void* stream);
+
 /* ------------------------------------------------------------------------
  * Dense-layer helpers of the model driver (not on the attention path).
  *

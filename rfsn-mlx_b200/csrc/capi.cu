@@ -348,6 +348,35 @@ rfsn_status rfsn_rope_append_step(const void* q, const void* k, const void* v, i
                               step_state, step_state_copy);
 }
 
+rfsn_status rfsn_rope_append_tables(const void* q, const void* k, const void* v, int in_dtype, const void* cos_t,
+                                    const void* sin_t, int tab_dtype, const float* inv_freq, int pos0, int batch,
+                                    int q_heads, int kv_heads, int len, int head_dim, float* q_out,
+                                    const rfsn_arena* arena, int ring_row0, int capacity, int write_index,
+                                    void* stream) {
+    RFSN_CHECK_ARG(arena != nullptr, "rfsn_rope_append_tables: NULL arena");
+    RFSN_CHECK_ARG(q != nullptr && k != nullptr && v != nullptr && q_out != nullptr,
+                   "rfsn_rope_append_tables: NULL q/k/v/q_out");
+    RFSN_CHECK_ARG((cos_t == nullptr) == (sin_t == nullptr), "rfsn_rope_append_tables: cos and sin go together");
+    RFSN_CHECK_ARG(cos_t != nullptr || inv_freq != nullptr, "rfsn_rope_append_tables: no tables and no inv_freq");
+    RFSN_CHECK_ARG(valid_dtype(in_dtype) && valid_dtype(tab_dtype), "rfsn_rope_append_tables: unknown dtype");
+    RFSN_CHECK_ARG(in_dtype == arena->dtype, "rfsn_rope_append_tables: input dtype %d differs from cache dtype %d",
+                   in_dtype, arena->dtype);
+    RFSN_CHECK_ARG(batch > 0 && q_heads > 0 && kv_heads > 0 && len > 0, "rfsn_rope_append_tables: non-positive shape");
+    RFSN_CHECK_ARG(head_dim == arena->head_dim && batch * kv_heads == arena->groups,
+                   "rfsn_rope_append_tables: shape does not match the arena");
+    RFSN_CHECK_ARG(capacity > 0 && ring_row0 >= 0 && ring_row0 + capacity <= arena->rows,
+                   "rfsn_rope_append_tables: ring rows outside the arena");
+    RFSN_CHECK_ARG(write_index >= 0 && write_index < capacity, "rfsn_rope_append_tables: write_index %d outside [0, %d)",
+                   write_index, capacity);
+    if (len > capacity) {
+        set_error("append_exact: chunk of %d tokens exceeds the ring capacity %d", len, capacity);
+        return RFSN_ERR_OVERFLOW;
+    }
+    return rope_tables_append_launch(in_dtype, tab_dtype, q, k, v, cos_t, sin_t, inv_freq, pos0, batch, q_heads,
+                                     kv_heads, len, head_dim, q_out, arena->k, arena->v, arena->rows, ring_row0,
+                                     capacity, write_index, static_cast<cudaStream_t>(stream));
+}
+
 rfsn_status rfsn_rms_norm(const void* x, const void* residual, const void* weight, void* sum_out, void* out, int rows,
                           int n, int dtype, float eps, void* stream) {
     RFSN_CHECK_ARG(x != nullptr && weight != nullptr && out != nullptr, "rfsn_rms_norm: NULL pointer");

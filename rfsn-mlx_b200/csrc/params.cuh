@@ -98,6 +98,11 @@ rfsn_status rope_append_launch(int dtype, const void* q, const void* k, const vo
                                int batch, int q_heads, int kv_heads, int len, int head_dim, float* q_out, void* ak,
                                void* av, int rows, int ring_row0, int capacity, int write_index, cudaStream_t stream,
                                const int* step_state = nullptr, int* step_state_copy = nullptr);
+rfsn_status rope_tables_append_launch(int dtype, int tab_dtype, const void* q, const void* k, const void* v,
+                                      const void* cos_t, const void* sin_t, const float* inv_freq, int pos0,
+                                      int batch, int q_heads, int kv_heads, int len, int head_dim, float* q_out,
+                                      void* ak, void* av, int rows, int ring_row0, int capacity, int write_index,
+                                      cudaStream_t stream);
 rfsn_status copy_rows_launch(void* ak, void* av, int groups, int rows, int row_bytes, int src_row0, int src_offset,
                              int src_wrap, int dst_row0, int count, cudaStream_t stream);
 

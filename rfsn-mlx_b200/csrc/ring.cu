@@ -1,4 +1,6 @@
 // Hot-ring kernels: fused RoPE + append, and arena row copies (seal).
+#include <type_traits>
+
 #include "params.cuh"
 
 namespace rfsn {
@@ -80,6 +82,70 @@ __global__ void rope_append_kernel(const TIn* __restrict__ q, const TIn* __restr
     }
 }
 
+// RoPE from explicit tables, then the append (layer.py:118-135 when the caller
+// passes rope_tables, or when the layer builds them in the model dtype). One
+// thread per (tensor row, pair j); the tables are [len][head_dim] rows of
+// positions pos0 + l and each half uses its own columns, as _apply_rope reads
+// them (layer.py:38-51):
+//   out[j]        = x1 * cos[l][j]        - x2 * sin[l][j]
+//   out[j + half] = x1 * sin[l][j + half] + x2 * cos[l][j + half]
+// Every product and sum is rounded to the promoted dtype of x and the tables
+// (the 16-bit type when both are that type, else float32), the way the
+// reference's elementwise ops round each result. Without tables (cos_t NULL)
+// they are built from inv_freq in float32 and rounded to TTab
+// (build_rope_tables with dtype = the table dtype).
+template <typename TIn, typename TTab>
+__global__ void rope_tables_append_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k,
+                                          const TIn* __restrict__ v, const TTab* __restrict__ cos_t,
+                                          const TTab* __restrict__ sin_t, const float* __restrict__ inv_freq, int pos0,
+                                          int batch, int q_heads, int kv_heads, int len, int head_dim,
+                                          float* __restrict__ q_out, TIn* __restrict__ ak, TIn* __restrict__ av,
+                                          int rows, int ring_row0, int capacity, int write_index) {
+    constexpr bool kRound16 = std::is_same<TIn, TTab>::value && !std::is_same<TIn, float>::value;
+    auto rnd = [](float x) { return kRound16 ? to_f32<TIn>(from_f32<TIn>(x)) : x; };
+    griddep_wait();
+    const int half = head_dim >> 1;
+    const long q_rows = (long)batch * q_heads * len;
+    const long kv_rows = (long)batch * kv_heads * len;
+    const long total = (q_rows + kv_rows) * half;
+    for (long idx = blockIdx.x * (long)blockDim.x + threadIdx.x; idx < total; idx += (long)gridDim.x * blockDim.x) {
+        const long r = idx / half;
+        const int j = (int)(idx - r * half);
+        const bool is_q = r < q_rows;
+        const long rr = is_q ? r : r - q_rows;
+        const int l = (int)(rr % len);
+        const TIn* src = is_q ? q : k;
+        const float x1 = to_f32<TIn>(src[rr * head_dim + j]);
+        const float x2 = to_f32<TIn>(src[rr * head_dim + j + half]);
+        float c_lo, s_lo, c_hi, s_hi;
+        if (cos_t != nullptr) {
+            c_lo = to_f32<TTab>(cos_t[(long)l * head_dim + j]);
+            s_lo = to_f32<TTab>(sin_t[(long)l * head_dim + j]);
+            c_hi = to_f32<TTab>(cos_t[(long)l * head_dim + j + half]);
+            s_hi = to_f32<TTab>(sin_t[(long)l * head_dim + j + half]);
+        } else {
+            const float f = __fmul_rn((float)(pos0 + l), inv_freq[j]);
+            c_lo = c_hi = to_f32<TTab>(from_f32<TTab>(cosf(f)));
+            s_lo = s_hi = to_f32<TTab>(from_f32<TTab>(sinf(f)));
+        }
+        const float o1 = rnd(__fsub_rn(rnd(__fmul_rn(x1, c_lo)), rnd(__fmul_rn(x2, s_lo))));
+        const float o2 = rnd(__fadd_rn(rnd(__fmul_rn(x1, s_hi)), rnd(__fmul_rn(x2, c_hi))));
+        if (is_q) {
+            q_out[rr * head_dim + j] = o1;
+            q_out[rr * head_dim + j + half] = o2;
+        } else {
+            const long bh = rr / len;
+            const int slot = (write_index + l) % capacity;
+            const long dst = (bh * rows + ring_row0 + slot) * head_dim;
+            ak[dst + j] = from_f32<TIn>(o1);
+            ak[dst + j + half] = from_f32<TIn>(o2);
+            av[dst + j] = v[rr * head_dim + j];
+            av[dst + j + half] = v[rr * head_dim + j + half];
+        }
+    }
+    griddep_launch_dependents();
+}
+
 // Copy `count` rows of every head from src (read modulo src_wrap when > 0)
 // to dst, 16 bytes per thread step, for K and V. Source and destination
 // row ranges must not overlap (seal copies ring rows into block rows).
@@ -131,12 +197,70 @@ rfsn_status rope_append_launch(int dtype, const void* q, const void* k, const vo
     return RFSN_OK;
 }
 
+template <typename TIn>
+static rfsn_status rope_tables_launch_in(int tab_dtype, const void* q, const void* k, const void* v, const void* cos_t,
+                                         const void* sin_t, const float* inv_freq, int pos0, int batch, int q_heads,
+                                         int kv_heads, int len, int head_dim, float* q_out, void* ak, void* av,
+                                         int rows, int ring_row0, int capacity, int write_index, dim3 grid,
+                                         cudaStream_t stream) {
+#define RFSN_ROPE_TAB_LAUNCH(TT)                                                                                  \
+    RFSN_CUDA(launch_pdl(ring::rope_tables_append_kernel<TIn, TT>, grid, dim3(256), 0, stream,                    \
+                         static_cast<const TIn*>(q), static_cast<const TIn*>(k), static_cast<const TIn*>(v),       \
+                         static_cast<const TT*>(cos_t), static_cast<const TT*>(sin_t), inv_freq, pos0, batch,     \
+                         q_heads, kv_heads, len, head_dim, q_out, static_cast<TIn*>(ak), static_cast<TIn*>(av),  \
+                         rows, ring_row0, capacity, write_index))
+    if (tab_dtype == RFSN_F32) {
+        RFSN_ROPE_TAB_LAUNCH(float);
+    } else if (tab_dtype == RFSN_F16) {
+        RFSN_ROPE_TAB_LAUNCH(__half);
+    } else {
+        RFSN_ROPE_TAB_LAUNCH(__nv_bfloat16);
+    }
+#undef RFSN_ROPE_TAB_LAUNCH
+    return RFSN_OK;
+}
+
+rfsn_status rope_tables_append_launch(int dtype, int tab_dtype, const void* q, const void* k, const void* v,
+                                      const void* cos_t, const void* sin_t, const float* inv_freq, int pos0,
+                                      int batch, int q_heads, int kv_heads, int len, int head_dim, float* q_out,
+                                      void* ak, void* av, int rows, int ring_row0, int capacity, int write_index,
+                                      cudaStream_t stream) {
+    const long total = ((long)batch * (q_heads + kv_heads) * len) * (head_dim / 2);
+    long blocks = (total + 255) / 256;
+    if (blocks > 65535L * 8) blocks = 65535L * 8;
+    if (blocks < 1) blocks = 1;
+    const dim3 grid((unsigned)blocks);
+    rfsn_status st;
+    if (dtype == RFSN_F32) {
+        st = rope_tables_launch_in<float>(tab_dtype, q, k, v, cos_t, sin_t, inv_freq, pos0, batch, q_heads, kv_heads,
+                                          len, head_dim, q_out, ak, av, rows, ring_row0, capacity, write_index, grid,
+                                          stream);
+    } else if (dtype == RFSN_F16) {
+        st = rope_tables_launch_in<__half>(tab_dtype, q, k, v, cos_t, sin_t, inv_freq, pos0, batch, q_heads, kv_heads,
+                                           len, head_dim, q_out, ak, av, rows, ring_row0, capacity, write_index, grid,
+                                           stream);
+    } else {
+        st = rope_tables_launch_in<__nv_bfloat16>(tab_dtype, q, k, v, cos_t, sin_t, inv_freq, pos0, batch, q_heads,
+                                                  kv_heads, len, head_dim, q_out, ak, av, rows, ring_row0, capacity,
+                                                  write_index, grid, stream);
+    }
+    if (st != RFSN_OK) return st;
+    RFSN_CUDA(cudaGetLastError());
+    note_launch();
+    return RFSN_OK;
+}
+
 void preload_ring_kernels() {
     cudaFuncAttributes a;
     cudaFuncGetAttributes(&a, ring::rope_append_kernel<float, float>);
     cudaFuncGetAttributes(&a, ring::rope_append_kernel<__half, __half>);
     cudaFuncGetAttributes(&a, ring::rope_append_kernel<__nv_bfloat16, __nv_bfloat16>);
     cudaFuncGetAttributes(&a, ring::copy_rows_kernel);
+    cudaFuncGetAttributes(&a, ring::rope_tables_append_kernel<__nv_bfloat16, __nv_bfloat16>);
+    cudaFuncGetAttributes(&a, ring::rope_tables_append_kernel<__nv_bfloat16, float>);
+    cudaFuncGetAttributes(&a, ring::rope_tables_append_kernel<__half, __half>);
+    cudaFuncGetAttributes(&a, ring::rope_tables_append_kernel<__half, float>);
+    cudaFuncGetAttributes(&a, ring::rope_tables_append_kernel<float, float>);
 }
 
 rfsn_status copy_rows_launch(void* ak, void* av, int groups, int rows, int row_bytes, int src_row0, int src_offset,

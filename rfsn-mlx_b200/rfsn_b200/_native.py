@@ -47,6 +47,7 @@ EXPORTED_SYMBOLS = (
     "rfsn_arena_destroy",
     "rfsn_rope_append",
     "rfsn_rope_append_step",
+    "rfsn_rope_append_tables",
     "rfsn_arena_copy_rows",
     "rfsn_block_upload",
     "rfsn_block_download",
@@ -147,6 +148,8 @@ def load_library() -> ctypes.CDLL:
         "rfsn_arena_destroy": (i32, [vp]),
         "rfsn_rope_append": (i32, [vp, vp, vp, i32, vp, i32, i32, i32, i32, i32, i32, vp, vp, i32, i32, i32, vp]),
         "rfsn_rope_append_step": (i32, [vp, vp, vp, i32, vp, vp, vp, i32, i32, i32, i32, i32, vp, vp, i32, i32, vp]),
+        "rfsn_rope_append_tables": (i32, [vp, vp, vp, i32, vp, vp, i32, vp, i32, i32, i32, i32, i32, i32, vp, vp, i32,
+                                          i32, i32, vp]),
         "rfsn_host_device_pointer": (i32, [vp, ctypes.POINTER(ctypes.c_void_p)]),
         "rfsn_prefill_plan": (i32, [i32] * 8 + [ctypes.POINTER(ctypes.c_int)] * 3),
         "rfsn_rms_norm": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, ctypes.c_float, vp]),

@@ -175,6 +175,22 @@ class DeviceOps:
         )
         return q_out
 
+    def append_tables(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cos_t: Optional[torch.Tensor],
+                      sin_t: Optional[torch.Tensor], table_dtype: torch.dtype, inv_freq: torch.Tensor, start_pos: int,
+                      capacity: int, write_index: int) -> torch.Tensor:
+        B, Hkv, L, D = (int(x) for x in k.shape)
+        q_out = torch.empty(q.shape, dtype=torch.float32, device=self.device)
+        native.check(
+            native.lib().rfsn_rope_append_tables(
+                q.data_ptr(), k.data_ptr(), v.data_ptr(), native.dtype_code(k.dtype),
+                cos_t.data_ptr() if cos_t is not None else None, sin_t.data_ptr() if sin_t is not None else None,
+                native.dtype_code(table_dtype), inv_freq.data_ptr(), int(start_pos), B, int(q.shape[1]), Hkv, L, D,
+                q_out.data_ptr(), self.arena.handle, 0, capacity, write_index, native.stream_ptr(),
+            ),
+            "rfsn_rope_append_tables",
+        )
+        return q_out
+
     def rotate_q(self, q: torch.Tensor, inv_freq: torch.Tensor, start_pos: int) -> torch.Tensor:
         B, H, L, D = (int(x) for x in q.shape)
         q_out = torch.empty(q.shape, dtype=torch.float32, device=self.device)
@@ -746,6 +762,38 @@ class LayerKVCache:
         kc, vc = self._kv_arg(k), self._kv_arg(v)
         q_out = self._ops.append(qc, kc, vc, self.inv_freq(), int(start_pos), self.config.hot_capacity,
                                  self.hot_write_index)
+        self.hot_seq_len += seq_len
+        return q_out
+
+    def append_rope_tables(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, start_pos: int,
+                           rope_tables: Optional[tuple] = None) -> torch.Tensor:
+        """layer.py:118-135 for a layer called with ``rope_tables``, or without
+        them: RoPE from the given (cos, sin) tables ([L, D] each, used as given)
+        or from tables built in the model dtype (build_rope_tables with
+        dtype = the model dtype), every product and sum rounded to the promoted
+        dtype of q/k and the tables; then the append. Returns the rotated q as
+        float32 (holding values of that promoted dtype)."""
+        seq_len = int(k.shape[2])
+        D = self.config.head_dim
+        cos_t = sin_t = None
+        table_dtype = self.dtype
+        if rope_tables is not None:
+            cos_t, sin_t = rope_tables
+            if not (isinstance(cos_t, torch.Tensor) and isinstance(sin_t, torch.Tensor)):
+                raise ValueError("rope_tables must be a (cos, sin) pair of tensors")
+            if cos_t.dtype != sin_t.dtype or cos_t.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+                raise ValueError("rope_tables: cos and sin must share one float dtype (float32, float16, bfloat16)")
+            if tuple(cos_t.shape[-2:]) != (seq_len, D) or tuple(sin_t.shape[-2:]) != (seq_len, D) or \
+                    cos_t.numel() != seq_len * D or sin_t.numel() != seq_len * D:
+                raise ValueError(f"rope_tables must be [{seq_len}, {D}] (one row per new position)")
+            table_dtype = cos_t.dtype
+            cos_t = cos_t.to(self.device).reshape(seq_len, D).contiguous()
+            sin_t = sin_t.to(self.device).reshape(seq_len, D).contiguous()
+        self._check_append(seq_len)
+        qc = _as(q, self.device, self.dtype)
+        kc, vc = self._kv_arg(k), self._kv_arg(v)
+        q_out = self._ops.append_tables(qc, kc, vc, cos_t, sin_t, table_dtype, self.inv_freq(), int(start_pos),
+                                        self.config.hot_capacity, self.hot_write_index)
         self.hot_seq_len += seq_len
         return q_out
 

@@ -49,6 +49,21 @@ def attention_step(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cache: Lay
     return paged_attention(cache, q_rot, start_pos, segments)
 
 
+def attention_step_tables(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cache: LayerKVCache, start_pos: int,
+                          rope_tables=None) -> torch.Tensor:
+    """``attention_step`` with the RoPE of a stand-alone layer call
+    (layer.py:118-135): the given (cos, sin) tables, or tables built in the
+    model dtype when ``rope_tables`` is None, with the reference's per-op
+    rounding. Returns the float32 attention output [B, H, L, D]."""
+    seq_len = int(k.shape[2])
+    cache.evict_for_append(seq_len)
+    q_rot = cache.append_rope_tables(q, k, v, start_pos, rope_tables)
+    if seq_len == 1:
+        cache.maybe_prefetch_for_decode(start_pos)
+    segments = cache.get_attention_segments()
+    return paged_attention(cache, q_rot, start_pos, segments)
+
+
 def capture_graph(fn, stream: torch.cuda.Stream) -> torch.cuda.CUDAGraph:
     """Capture ``fn()`` into a new CUDA graph on ``stream``. Unlike the
     ``torch.cuda.graph`` context manager this runs no garbage collection or

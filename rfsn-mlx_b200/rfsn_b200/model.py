@@ -31,7 +31,7 @@ import torch.nn.functional as F
 from . import _native as native
 from .cache import RFSNCache, _as, paged_attention
 from .config import RFSNConfig, RuntimeMode, resolve_dtype
-from .layer import attention_step, capture_graph
+from .layer import attention_step, attention_step_tables, capture_graph
 
 ArrayLike = Union[np.ndarray, torch.Tensor]
 
@@ -160,6 +160,18 @@ class _Weight:
         self.weight = weight
 
 
+class _ModelRopeTables:
+    """The float32 RoPE tables the model builds for its layers (model.py:120,
+    build_rope_tables with its default float32 dtype). The fused RoPE/append
+    kernel computes exactly those rotations, so the tables are not built."""
+
+    def __repr__(self) -> str:
+        return "MODEL_ROPE_TABLES"
+
+
+MODEL_ROPE_TABLES = _ModelRopeTables()
+
+
 class RFSNLayerNorm:
     """layer.py:53-64 RMS norm (no bias): ``weight`` (ones unless given) and
     ``eps``; ``norm(x)`` is weight * x / sqrt(mean(x^2) + eps) computed in float32
@@ -220,10 +232,14 @@ class RFSNLayer:
         return self.p[f"layers.{self.layer_idx}.{name}"]
 
     def __call__(self, x: torch.Tensor, cache, rope_tables=None, start_pos: int = 0, attn=None) -> torch.Tensor:
-        """layer.py:97-167. ``rope_tables`` is accepted for the reference's call
-        signature; the rotation is computed in the fused RoPE/append kernel from
-        the cache's frequency table. ``attn(q, k, v)`` replaces the attention
-        step (used by the captured decode graph)."""
+        """layer.py:97-167. RoPE as the reference's layer applies it:
+        ``rope_tables=MODEL_ROPE_TABLES`` (what ``RFSNModel`` passes: the float32
+        tables of model.py:120) rotates in float32 inside the fused RoPE/append
+        kernel; a (cos, sin) pair of tensors is used as given; None builds the
+        tables in the model dtype (layer.py:118-126), with each product and sum
+        rounded to the promoted dtype (for a float32 model that is the fused
+        float32 path). ``attn(q, k, v)`` replaces the attention step (used by
+        the captured decode graph)."""
         layer_cache = cache
         cfg = self.config
         B, L, _ = x.shape
@@ -234,7 +250,12 @@ class RFSNLayer:
         q = qkv[..., :H * D].reshape(B, L, H, D).transpose(1, 2)
         k = qkv[..., H * D:(H + Hkv) * D].reshape(B, L, Hkv, D).transpose(1, 2)
         v = qkv[..., (H + Hkv) * D:].reshape(B, L, Hkv, D).transpose(1, 2)
-        a = attention_step(q, k, v, layer_cache, start_pos) if attn is None else attn(q, k, v)  # float32 [B, H, L, D]
+        if attn is not None:
+            a = attn(q, k, v)  # float32 [B, H, L, D]
+        elif rope_tables is MODEL_ROPE_TABLES or (rope_tables is None and layer_cache.dtype == torch.float32):
+            a = attention_step(q, k, v, layer_cache, start_pos)
+        else:
+            a = attention_step_tables(q, k, v, layer_cache, start_pos, rope_tables)
         attn = a.transpose(1, 2).reshape(B, L, H * D).to(x.dtype)
         x, h = _add_rms_norm(_linear(attn, self._w("o_proj.weight")), residual, self._w("ffn_norm.weight"),
                              cfg.norm_eps)
@@ -340,7 +361,7 @@ class RFSNModel:
     def _forward(self, x: torch.Tensor, cache: RFSNCache, start_pos: int) -> torch.Tensor:
         """model.py:106-131."""
         for i, layer in enumerate(self.layers):
-            x = layer(x, cache.layer(i), start_pos=start_pos)
+            x = layer(x, cache.layer(i), rope_tables=MODEL_ROPE_TABLES, start_pos=start_pos)
         x = _layer_norm(x, self.params["norm.weight"], self.params["norm.bias"], self.config.norm_eps)
         return self._lm_head(x)
 

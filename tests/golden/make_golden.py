@@ -19,6 +19,9 @@ are:
   plus EXACT-mode errors.
 * ``residency_trace.json`` warm/cold residency, prefetch and metrics for a
   small warm capacity (the reference's prefetch test scenario, extended).
+* ``rope_golden.npz``     the reference's ``build_rope_tables`` and
+  ``_apply_rope`` with tables in the model dtype or another dtype (the RoPE of
+  a layer called without tables, or with tables passed in).
 * ``tiny_model_golden.npz`` the CPU-runnable tiny model (1 layer, hidden 128,
   2/2 heads, head_dim 64, SwiGLU 4x, vocab 128, tied head, theta 1e4, fp32,
   hot 8 / block 4): prompt of 8 ids (seed 1) + 8 greedy decode steps, with
@@ -322,6 +325,38 @@ def make_tiny_model(mx, out_path: Path) -> None:
         np.savez_compressed(out_path, **blobs)
 
 
+ROPE_CASES = [
+    # name, x dtype, table dtype, heads, L, D, start position, base
+    ("bf16_tables_bf16", "bfloat16", "bfloat16", 4, 5, 128, 131000, 500000.0),
+    ("bf16_tables_f32", "bfloat16", "float32", 4, 3, 128, 4093, 1e6),
+    ("f16_tables_f16", "float16", "float16", 2, 4, 64, 70, 10000.0),
+    ("f16_tables_bf16", "float16", "bfloat16", 2, 2, 128, 30000, 500000.0),
+    ("f32_tables_bf16", "float32", "bfloat16", 2, 3, 64, 9, 10000.0),
+]
+
+
+def make_rope(mx, out_path: Path) -> None:
+    from rfsn_v10_5.layer import _apply_rope, build_rope_tables
+
+    rng = np.random.default_rng(20240607)
+    blobs: dict[str, np.ndarray] = {}
+    for name, xd, td, H, L, D, start, base in ROPE_CASES:
+        x32 = rng.standard_normal((1, H, L, D)).astype(np.float32)
+        x = mx.array(x32).astype(getattr(mx, xd))  # layer.py:116-118: q/k in the model dtype
+        cos_t, sin_t = build_rope_tables(D, base, L, start_pos=start, dtype=getattr(mx, td))
+        out = _apply_rope(x, cos_t, sin_t)
+        f32 = lambda a: np.array(a.astype(mx.float32))  # noqa: E731
+        blobs[f"{name}/x"] = _storage(f32(x), xd)
+        blobs[f"{name}/cos"] = _storage(f32(cos_t), td)
+        blobs[f"{name}/sin"] = _storage(f32(sin_t), td)
+        blobs[f"{name}/out"] = f32(out)
+        blobs[f"{name}/meta"] = np.array([H, L, D, start], np.int64)
+        blobs[f"{name}/base"] = np.array(base, np.float64)
+        blobs[f"{name}/dtypes"] = np.array([xd, td, str(out.dtype).split(".")[-1]])
+    blobs["__cases__"] = np.array([c[0] for c in ROPE_CASES])
+    np.savez_compressed(out_path, **blobs)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("RFSN_REFERENCE", "/root/reference"))
@@ -335,6 +370,7 @@ def main() -> None:
     make_ring_traces(mx, out / "ring_traces.json")
     make_residency_trace(mx, out / "residency_trace.json")
     make_tiny_model(mx, out / "tiny_model_golden.npz")
+    make_rope(mx, out / "rope_golden.npz")
     for p in sorted(out.iterdir()):
         if p.suffix in (".npz", ".json"):
             print(f"{p.name}: {p.stat().st_size} bytes")

@@ -4,6 +4,7 @@ reference's own modules (tests/golden/make_golden.py)."""
 import numpy as np
 import pytest
 
+from _util import GOLDEN as GOLDEN_DIR
 from _util import golden_attention_cases, load_json
 from oracle.kv_ring import RingOracle
 from oracle.numerics import bf16_bits_to_f32, f32_to_bf16_bits, from_storage
@@ -47,6 +48,28 @@ def test_oracle_rows_at_explicit_positions_equal_the_contiguous_chunk(case):
                                              q_positions=[case["q_start"] + r for r in rows])
     np.testing.assert_allclose(part, full[:, :, rows], atol=2e-6, rtol=0)
     np.testing.assert_allclose(part_lse, full_lse[:, :, rows], atol=2e-6, rtol=1e-6)
+
+
+ROPE = np.load(GOLDEN_DIR / "rope_golden.npz")
+
+
+@pytest.mark.parametrize("name", [str(n) for n in ROPE["__cases__"]])
+def test_oracle_rope_in_table_dtype_matches_reference(name):
+    """The rotation with tables in the model dtype or another dtype, every op
+    rounded to the promoted dtype, equals the reference's _apply_rope bit for
+    bit; the tables agree to the float32 trig and inv_freq ulps (scaled by the
+    position, since inv_freq's last bit moves the angle by position x ulp)."""
+    from oracle.rope import apply_rope_in, promoted_dtype, rope_tables_in
+
+    xd, td, _ = (str(x) for x in ROPE[f"{name}/dtypes"])
+    H, L, D, start = (int(x) for x in ROPE[f"{name}/meta"])
+    x = from_storage(ROPE[f"{name}/x"], xd)
+    c = from_storage(ROPE[f"{name}/cos"], td)
+    s = from_storage(ROPE[f"{name}/sin"], td)
+    np.testing.assert_array_equal(apply_rope_in(x, c, s, promoted_dtype(xd, td)), ROPE[f"{name}/out"])
+    c2, s2 = rope_tables_in(D, float(ROPE[f"{name}/base"]), L, start, td)
+    bound = (start + L) * 2.0 ** -23 * 2 + {"float32": 0.0, "bfloat16": 2.0 ** -8, "float16": 2.0 ** -11}[td]
+    assert np.abs(c2 - c).max() <= bound and np.abs(s2 - s).max() <= bound
 
 
 RING = load_json("ring_traces.json")

@@ -98,7 +98,7 @@ def _noalloc_check():
         ("bfloat16", 1, 32, 8, 1, 128, [1000] * 12 + [24]),  # tensor-core kernel
         ("float16", 1, 32, 8, 1, 128, [256] * 6),
         ("float32", 1, 4, 2, 3, 64, [37, 64, 5]),              # CUDA-core kernel
-        ("float16", 1, 32, 8, 1024, 128, [64, 64]),            # tensor-core prefill: no partials when unsplit
+        ("float16", 1, 32, 8, 1024, 128, [512, 512]),          # tensor-core prefill: no partials when unsplit
     ],
 )
 def test_noalloc_matches_workspace_entry_point_twice(dtype, B, H, Hkv, Lq, D, blocks):
