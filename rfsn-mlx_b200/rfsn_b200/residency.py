@@ -1,40 +1,46 @@
-"""Warm-set sizing and sequential prefetch (drop-in for ``rfsn_v10_5.residency``).
+"""Warm-set bound and one-block sequential prefetch for one layer's blocks.
 
-Policy identical to the reference (residency.py:26-156) so residency
-decisions and metrics match bit for bit:
+Drop-in for ``rfsn_v10_5.residency`` (residency.py:26-156): the decisions
+and the counters are the reference's, so residency traces replay bit for bit.
 
-* warm set bounded by ``warm_capacity`` tokens; the victim is the eligible
-  (warm, materializable, unpinned, not protected) block with the smallest
-  ``(last_accessed_at, logical_start)`` and is demoted to the cold tier;
-* one-block sequential prefetch: the cold block right after the warm
-  frontier once ``query_pos >= warm.logical_end - margin``, else the cold
-  block right before a warm block under the same condition;
-* completions are consumed on the caller's thread.
+* Demotion: while the warm set holds more than ``warm_capacity`` tokens, the
+  warm, materializable, unpinned block (other than a protected one) with the
+  smallest ``(last_accessed_at, logical_start)`` goes to the cold tier.
+* Prefetch: along the layer's materializable blocks in page-table order, the
+  first warm -> cold boundary whose warm block the query has (nearly) reached
+  (``query_pos >= logical_end - margin``) names the cold block after it; failing
+  that, the first cold -> warm boundary whose warm block is reached names the
+  cold block before it. One load per block in flight, on one worker thread.
+* Completions are applied on the caller's thread when it next drains them.
 
-What changes is the data path. The worker thread reads, verifies and
-decompresses the cold payload (numpy, off the caller's thread). When the
-caller drains it, the payload is staged in pinned host memory and copied into
-the device arena with an asynchronous host-to-device copy on a side stream;
-the compute stream waits on that copy's event before its next kernel.
-One exact shortcut: a decode-step prefetch check on a layer without any cold
-block returns at once (both candidate rules need a cold block); when every
-live block is resident in HBM that is known without a scan.
+The pieces are separate here: two pure decision functions over manifests
+(``demotion_victim`` and ``prefetch_target``, one pass each), a small queue of
+loads in flight (``_LoadQueue``), and the manager that applies their outcomes
+to the cache. The data path is this package's: the worker reads, verifies
+and decompresses a cold payload; applying it stages the payload in pinned
+memory and copies it into the device arena on a side stream, which the
+compute stream waits on before its next kernel. A layer with no cold block
+skips the prefetch scan (both rules need one).
 """
 
 from __future__ import annotations
 
 from concurrent.futures import Future, ThreadPoolExecutor
 from dataclasses import asdict, dataclass
-from typing import TYPE_CHECKING, Optional
+from typing import TYPE_CHECKING, Callable, Iterator, Optional, Sequence
 
 from .block_manager import BlockId, BlockLocation, BlockManifest
 
 if TYPE_CHECKING:
     from .cache import LayerKVCache
 
+_WARM, _COLD = BlockLocation.WARM_RAM, BlockLocation.COLD_DISK
+
 
 @dataclass
 class ResidencyMetrics:
+    """Counters of residency.py:26-33 (same names, reported by get_metrics)."""
+
     warm_evictions: int = 0
     prefetch_requests: int = 0
     prefetch_completions: int = 0
@@ -43,109 +49,136 @@ class ResidencyMetrics:
     unmaterializable_blocks: int = 0
 
 
+def demotion_victim(manifests: Sequence[BlockManifest], protected: Optional[BlockId] = None) -> Optional[BlockManifest]:
+    """The block a full warm set gives up: least recently used among the
+    demotable ones, ties broken by the earlier position (residency.py:51-66)."""
+    best: Optional[tuple] = None
+    for m in manifests:
+        if m.residency != _WARM or not m.materializable or m.pin_count or m.block_id == protected:
+            continue
+        rank = (m.last_accessed_at, m.logical_start)
+        if best is None or rank < best[0]:
+            best = (rank, m)
+    return None if best is None else best[1]
+
+
+def prefetch_target(blocks: Sequence[BlockManifest], query_pos: int, margin: int) -> Optional[BlockManifest]:
+    """The cold block to load next for a query at ``query_pos`` (residency.py:85-130),
+    found in one walk over adjacent pairs: a warm -> cold boundary whose warm
+    side is reached wins at once; otherwise the first cold -> warm boundary
+    whose warm side is reached."""
+    behind: Optional[BlockManifest] = None
+    for left, right in zip(blocks, blocks[1:]):
+        if left.residency == _WARM and right.residency == _COLD:
+            if query_pos >= left.logical_end - margin:
+                return right
+        elif behind is None and left.residency == _COLD and right.residency == _WARM:
+            if query_pos >= right.logical_end - margin:
+                behind = left
+    return behind
+
+
+class _LoadQueue:
+    """Cold-payload loads on one worker thread, keyed by block."""
+
+    def __init__(self) -> None:
+        self._pool = ThreadPoolExecutor(max_workers=1, thread_name_prefix="rfsn-prefetch")
+        self._inflight: dict[BlockId, Future] = {}
+
+    def __len__(self) -> int:
+        return len(self._inflight)
+
+    def __contains__(self, block_id: BlockId) -> bool:
+        return block_id in self._inflight
+
+    def submit(self, block_id: BlockId, load: Callable, manifest: BlockManifest) -> None:
+        self._inflight[block_id] = self._pool.submit(load, manifest)
+
+    def finished(self) -> Iterator[tuple[BlockId, Future]]:
+        """Loads that are done when the walk reaches them, oldest first, each
+        handed out once (loads submitted meanwhile wait for the next walk)."""
+        for block_id, future in list(self._inflight.items()):
+            if future.done():
+                del self._inflight[block_id]
+                yield block_id, future
+
+    def wait_all(self, timeout: float) -> None:
+        for future in list(self._inflight.values()):
+            future.result(timeout=timeout)
+
+    def clear(self) -> None:
+        for future in self._inflight.values():
+            future.cancel()
+        self._inflight.clear()
+
+
 class ResidencyManager:
-    """Manage warm-set sizing and simple sequential prefetch."""
+    """Manage warm-set sizing and sequential prefetch of one layer's blocks."""
 
     def __init__(self, *, prefetch_margin_tokens: int = 1) -> None:
         self.prefetch_margin_tokens = max(1, prefetch_margin_tokens)
-        self._executor = ThreadPoolExecutor(max_workers=1, thread_name_prefix="rfsn-prefetch")
-        self._prefetch_futures: dict[BlockId, Future] = {}
+        self._loads = _LoadQueue()
         self.metrics = ResidencyMetrics()
 
     @property
     def has_pending(self) -> bool:
-        return bool(self._prefetch_futures)
+        return len(self._loads) > 0
 
     def reset(self) -> None:
-        for future in self._prefetch_futures.values():
-            future.cancel()
-        self._prefetch_futures.clear()
+        self._loads.clear()
         self.metrics = ResidencyMetrics()
 
     def choose_warm_eviction_victim(
         self, manifests: list[BlockManifest], *, protected_block_id: Optional[BlockId] = None
     ) -> Optional[BlockManifest]:
-        best: Optional[BlockManifest] = None
-        best_key = None
-        for m in manifests:
-            if (
-                m.residency != BlockLocation.WARM_RAM
-                or not m.materializable
-                or m.pin_count != 0
-                or m.block_id == protected_block_id
-            ):
-                continue
-            key = (m.last_accessed_at, m.logical_start)
-            if best_key is None or key < best_key:
-                best, best_key = m, key
-        return best
+        return demotion_victim(manifests, protected_block_id)
 
     def evict_warm_excess(self, cache: "LayerKVCache", *, protected_block_id: Optional[BlockId] = None) -> None:
-        while cache._warm_token_count() > cache.config.warm_capacity:
-            victim = self.choose_warm_eviction_victim(cache._warm_manifests(), protected_block_id=protected_block_id)
+        cap = cache.config.warm_capacity
+        while cache._warm_token_count() > cap:
+            victim = demotion_victim(cache._warm_manifests(), protected_block_id)
             if victim is None:
-                return
+                break
             cache.demote_manifest_to_cold(victim)
             self.metrics.warm_evictions += 1
 
     def maybe_schedule_prefetch(self, cache: "LayerKVCache", query_abs_pos: int) -> None:
         self.drain_completed_prefetches(cache)
+        if cache.all_blocks_resident():
+            return
         live = cache.block_manager.page_table.layer_entries(cache.layer_id)
-        # Both candidate rules need a cold block; with none, nothing can be scheduled.
-        # O(1) when every live block is resident in HBM, else a scan.
-        all_resident = getattr(cache, "all_blocks_resident", None)
-        if all_resident is not None and all_resident():
+        if all(m.residency != _COLD for m in live):
             return
-        if not any(m.residency == BlockLocation.COLD_DISK for m in live):
+        target = prefetch_target([m for m in live if m.materializable], query_abs_pos, self.prefetch_margin_tokens)
+        if target is None or target.block_id in self._loads or cache.is_manifest_resident(target):
             return
-        manifests = [m for m in live if m.materializable]
-        if len(manifests) < 2:
-            return
-        trigger = lambda m: query_abs_pos >= m.logical_end - self.prefetch_margin_tokens  # noqa: E731
-        candidate: Optional[BlockManifest] = None
-        for cur, nxt in zip(manifests, manifests[1:]):
-            if cur.residency == BlockLocation.WARM_RAM and nxt.residency == BlockLocation.COLD_DISK and trigger(cur):
-                candidate = nxt
-                break
-        if candidate is None:
-            for prev, cur in zip(manifests, manifests[1:]):
-                if prev.residency == BlockLocation.COLD_DISK and cur.residency == BlockLocation.WARM_RAM and trigger(cur):
-                    candidate = prev
-                    break
-        if candidate is None or candidate.block_id in self._prefetch_futures or cache.is_manifest_resident(candidate):
-            return
-        self._prefetch_futures[candidate.block_id] = self._executor.submit(cache.load_manifest_payload_only, candidate)
+        self._loads.submit(target.block_id, cache.load_manifest_payload_only, target)
         self.metrics.prefetch_requests += 1
 
     def drain_completed_prefetches(self, cache: "LayerKVCache") -> None:
-        if not self._prefetch_futures:
+        if not self.has_pending:
             return
-        for block_id, future in list(self._prefetch_futures.items()):
-            if not future.done():
-                continue
-            self._prefetch_futures.pop(block_id, None)
+        for block_id, future in self._loads.finished():
             manifest = cache.block_manager.get_block(block_id)
-            try:
-                payload = future.result()
-            except Exception as exc:  # the worker's failure becomes a MISSING block
-                cache.block_manager.mark_missing(block_id, reason=f"prefetch failed: {exc}")
-                cache._note_table_change()
+            error = future.exception()
+            if error is not None:
+                # a load that raised leaves the block MISSING (residency.py:131-134)
+                cache.block_manager.mark_missing(block_id, reason=f"prefetch failed: {error}")
                 self.metrics.missing_blocks += 1
-                continue
-            if payload is None:
-                if manifest.residency == BlockLocation.MISSING:
-                    self.metrics.missing_blocks += 1
-                if not manifest.materializable:
-                    self.metrics.unmaterializable_blocks += 1
-                cache._note_table_change()
-                continue
-            cache.promote_manifest_from_payload(manifest, payload)
-            self.evict_warm_excess(cache, protected_block_id=manifest.block_id)
-            self.metrics.prefetch_completions += 1
+            else:
+                payload = future.result()
+                if payload is not None:
+                    cache.promote_manifest_from_payload(manifest, payload)
+                    self.evict_warm_excess(cache, protected_block_id=block_id)
+                    self.metrics.prefetch_completions += 1
+                    continue
+                # no payload: the storage marked it missing or unreadable
+                self.metrics.missing_blocks += manifest.residency == BlockLocation.MISSING
+                self.metrics.unmaterializable_blocks += not manifest.materializable
+            cache._note_table_change()
 
     def wait_for_prefetches(self, cache: "LayerKVCache", *, timeout: float = 1.0) -> None:
-        for future in list(self._prefetch_futures.values()):
-            future.result(timeout=timeout)
+        self._loads.wait_all(timeout)
         self.drain_completed_prefetches(cache)
 
     def note_sync_load(self) -> None:
