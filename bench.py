@@ -341,36 +341,52 @@ def e2e_parity(full, w, e2e_info):
 
 
 # ------------------------------------------------------------------------------------ measurements
-def device_throughput(cache, w, world, steps, warmup, calls_per_step, *, collective: bool, peers=None):
-    """calls/s with inputs resident: CUDA-graph-captured calls, CUDA events."""
+L2_ROTATION_BYTES = 256e6  # more than twice the 126 MB L2: rotated shard copies are read from HBM every call
+
+
+def shard_copies(w, world: int, total_tokens: int) -> int:
+    """Copies of a rank's shard the calls rotate through, so that consecutive
+    calls of a rank never find its K/V in L2 (a decode step runs every other
+    layer's attention between two calls of one layer). The same on every rank."""
+    if world == 1:
+        return 1
+    per_rank = algorithmic_bytes(w, total_tokens) / world
+    return max(1, int(-(-L2_ROTATION_BYTES // per_rank)))
+
+
+def device_throughput(caches, w, world, steps, warmup, calls_per_step, *, collective: bool, peers=None):
+    """calls/s with inputs resident: CUDA-graph-captured calls, CUDA events.
+    Call i uses shard copy i % len(caches)."""
     import torch
 
     from rfsn_b200 import _native as native
     from rfsn_b200.cache import paged_attention
     from rfsn_b200.sharded import merge_across_ranks
 
+    cache = caches[0]
     total = cache.hot_start + cache.hot_seq_len
     q = torch.randn((1, w["q_heads"], 1, w["head_dim"]), device=cache.device, dtype=torch.float32)
     pos = total - 1
-    segs = cache.get_attention_segments()
+    segs = [c.get_attention_segments() for c in caches]
     use_coll = collective and world > 1
 
-    def one_call():
+    def one_call(i):
+        c, sg = caches[i % len(caches)], segs[i % len(caches)]
         if use_coll and peers is not None:
-            return paged_attention(cache, q, pos, segs, peers=peers)
+            return paged_attention(c, q, pos, sg, peers=peers)
         if use_coll:
-            out, lse = paged_attention(cache, q, pos, segs, want_lse=True)
+            out, lse = paged_attention(c, q, pos, sg, want_lse=True)
             return merge_across_ranks(out, lse)
-        return paged_attention(cache, q, pos, segs, want_lse=world > 1)
+        return paged_attention(c, q, pos, sg, want_lse=world > 1)
 
-    for _ in range(3):  # eager warm-up: sizes the workspace, sets kernel attributes
-        one_call()
+    for i in range(3 * len(caches)):  # eager warm-up: sizes the workspace, sets kernel attributes
+        one_call(i)
     torch.cuda.synchronize()
     before = native.launch_count()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
-        for _ in range(calls_per_step):
-            one_call()
+        for i in range(calls_per_step):
+            one_call(i)
     launches_per_step = native.launch_count() - before
     torch.cuda.synchronize()
     for _ in range(warmup):
@@ -392,14 +408,18 @@ def device_throughput(cache, w, world, steps, warmup, calls_per_step, *, collect
     return ms, launches_per_step * steps
 
 
-def e2e_throughput(cache, w, world, owns_hot, steps, calls_per_step, peers=None):
-    """calls/s through the public API with pinned host inputs and a host read-back every call."""
+def e2e_throughput(caches, w, world, owns_hot, steps, calls_per_step, peers=None):
+    """calls/s through the public API with pinned host inputs and a host
+    read-back every call. With several shard copies they act as layers: every
+    token is stepped through each copy in turn at the same position."""
     import torch
 
     from rfsn_b200 import _native as native
     from rfsn_b200.layer import GraphedDecodeStep
     from rfsn_b200.sharded import GraphedShardedDecodeStep, sharded_decode_step
 
+    cache = caches[0]
+    ncopy = len(caches)
     dt = cache.dtype
     H, Hkv, D = w["q_heads"], w["kv_heads"], w["head_dim"]
     gen = torch.Generator().manual_seed(7)
@@ -416,54 +436,57 @@ def e2e_throughput(cache, w, world, owns_hot, steps, calls_per_step, peers=None)
         dist.all_reduce(t)
         pos = int(t.item())
 
-    graphed = None
+    graphed = []
     if world == 1 or peers is not None:
         # one graph replay per call: H2D of the token's q (and k/v on the hot-window
         # owner), RoPE + append, paged attention (merged over NVLink when sharded),
         # D2H of the output (rfsn_b200.layer.GraphedDecodeStep /
         # rfsn_b200.sharded.GraphedShardedDecodeStep)
-        if world == 1:
-            graphed = GraphedDecodeStep(cache, H)
-        else:
-            graphed = GraphedShardedDecodeStep(cache, H, owns_hot=owns_hot, peers=peers)
-        graphed.q_host.copy_(q_h)
-        graphed.k_host.copy_(k_h)
-        graphed.v_host.copy_(v_h)
+        for c in caches:
+            g = GraphedDecodeStep(c, H) if world == 1 else GraphedShardedDecodeStep(c, H, owns_hot=owns_hot,
+                                                                                     peers=peers)
+            g.q_host.copy_(q_h)
+            g.k_host.copy_(k_h)
+            g.v_host.copy_(v_h)
+            graphed.append(g)
 
-    def call(p):
-        if graphed is not None:
-            graphed.step(p)
+    def call(i, p):
+        if graphed:
+            graphed[i % ncopy].step(p)
             return
-        q = q_h.to(cache.device, non_blocking=True)
-        k = k_h.to(cache.device, non_blocking=True)
-        v = v_h.to(cache.device, non_blocking=True)
-        out = sharded_decode_step(cache, q, k if owns_hot else None, v if owns_hot else None, p, owns_hot=owns_hot,
+        c = caches[i % ncopy]
+        q = q_h.to(c.device, non_blocking=True)
+        k = k_h.to(c.device, non_blocking=True)
+        v = v_h.to(c.device, non_blocking=True)
+        out = sharded_decode_step(c, q, k if owns_hot else None, v if owns_hot else None, p, owns_hot=owns_hot,
                                   peers=peers)
         out_h.copy_(out, non_blocking=True)
         torch.cuda.current_stream().synchronize()
 
-    for i in range(3):
-        call(pos + i)
+    for t in range(3):  # warm-up tokens
+        for j in range(ncopy):
+            call(j, pos + t)
     pos += 3
     barrier(world)
     before = native.launch_count()
-    replays0 = graphed.replays if graphed is not None else 0
+    replays0 = sum(g.replays for g in graphed)
+    tokens = -(-steps * calls_per_step // ncopy)
+    n = tokens * ncopy
     t0 = time.perf_counter()
-    n = steps * calls_per_step
     for i in range(n):
-        call(pos + i)
+        call(i, pos + i // ncopy)
     elapsed = time.perf_counter() - t0
     launches = native.launch_count() - before
-    if graphed is not None:  # kernels replayed inside the graph are not host launches
-        launches += graphed.graph_kernels * (graphed.replays - replays0)
+    if graphed:  # kernels replayed inside the graph are not host launches
+        launches += graphed[0].graph_kernels * (sum(g.replays for g in graphed) - replays0)
     barrier(world)
-    if graphed is not None:  # the replay copies the whole packed staging buffer (step state + q/k/v)
-        h2d = graphed.stage_host.numel() * graphed.stage_host.element_size()
+    if graphed:  # the replay copies the whole packed staging buffer (step state + q/k/v)
+        h2d = graphed[0].stage_host.numel() * graphed[0].stage_host.element_size()
     else:
         h2d = q_h.numel() * q_h.element_size() + (k_h.numel() * k_h.element_size() * 2 if owns_hot else 0)
     d2h = out_h.numel() * out_h.element_size()
-    last = (graphed.out_host if graphed is not None else out_h).clone()
-    info = (pos - 3, n + 3, q_h, k_h, v_h, last)  # every call made, for a replay check
+    last = (graphed[-1].out_host if graphed else out_h).clone()
+    info = (pos - 3, tokens + 3, q_h, k_h, v_h, last)  # every token appended, for a replay check
     return elapsed, n, launches, h2d, d2h, info
 
 
@@ -539,6 +562,9 @@ def run_ours(args, w):
     extra = args.steps * e2e_calls + 8
     E2E_EXTRA[0] = extra
     cache, owns_hot, local_tokens, total_tokens = build_shard(w, rank, world, device, extra)
+    # a shard smaller than L2 is rotated with copies of itself (same data)
+    caches = [cache] + [build_shard(w, rank, world, device, extra)[0]
+                        for _ in range(shard_copies(w, world, sum(w["blocks"]) + w["hot"]) - 1)]
     torch.cuda.synchronize()
 
     peers = None
@@ -549,9 +575,9 @@ def run_ours(args, w):
     peak, peak_kind = measured_peaks()
     sampler = ClockSampler(device.index).start()
     # kernel-only (local attention, no collective): roofline of the decode kernel
-    k_ms, _ = device_throughput(cache, w, world, args.steps, args.warmup, args.calls_per_step, collective=False)
+    k_ms, _ = device_throughput(caches, w, world, args.steps, args.warmup, args.calls_per_step, collective=False)
     # full call (local attention + all-gather + merge when N > 1)
-    ms, launches = device_throughput(cache, w, world, args.steps, args.warmup, args.calls_per_step, collective=True,
+    ms, launches = device_throughput(caches, w, world, args.steps, args.warmup, args.calls_per_step, collective=True,
                                      peers=peers)
     clocks = sampler.stop()
     ms = max_over_ranks(ms, world)
@@ -567,7 +593,7 @@ def run_ours(args, w):
     achieved = local_bytes / k_call_s / 1e9
 
     # e2e through the public API (appends the new token each call)
-    e_elapsed, e_n, e_launches, h2d, d2h, e2e_info = e2e_throughput(cache, w, world, owns_hot, args.steps, e2e_calls,
+    e_elapsed, e_n, e_launches, h2d, d2h, e2e_info = e2e_throughput(caches, w, world, owns_hot, args.steps, e2e_calls,
                                                                      peers)
     e_elapsed = max_over_ranks(e_elapsed, world)
     parity = None
@@ -636,7 +662,11 @@ def run_ours(args, w):
                 "desc": w["desc"],
                 "context_tokens": total_tokens,
                 "calls_per_step": args.calls_per_step,
-                "l2": f"inputs larger than L2: {algorithmic_bytes(w, total_tokens) / 1e6:.0f} MB of K/V per call",
+                "l2": (f"inputs larger than L2: {algorithmic_bytes(w, total_tokens) / 1e6:.0f} MB of K/V per call"
+                       if len(caches) == 1 else
+                       f"each rank rotates {len(caches)} copies of its {local_bytes / 1e6:.0f} MB shard "
+                       f"({len(caches) * local_bytes / 1e6:.0f} MB > L2); the end-to-end loop steps every token "
+                       "through the copies like layers"),
                 "parallelism": (f"context-sharded over {world} GPUs by archived block; LSE merge "
                                 + ("fused into the attention kernel over NVLink (CUDA IPC mailboxes)"
                                    if args.merge == "p2p" else "via NCCL all-gather + merge kernel"))

@@ -107,7 +107,7 @@ def test_attention_step_with_model_dtype_tables_matches_oracle(dtype):
             hot = list(c.get_hot_attention_segments())
             k_dev = torch.cat([s[0] for s in hot], dim=2)[:, :, -n:].float().cpu().numpy()
             diff = np.abs(k_dev - k_rot[:, :, sl])
-            assert float(np.mean(diff > 0)) <= 0.01, float(np.mean(diff > 0))
+            assert float(np.mean(diff > 0)) <= 0.03, float(np.mean(diff > 0))
             assert np.all(diff <= 4 * ulp * np.maximum(np.abs(k_rot[:, :, sl]), 1.0))
             pos += n
         assert c.get_block_stats()["total_blocks"] > 0
