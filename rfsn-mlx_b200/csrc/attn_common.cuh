@@ -362,7 +362,9 @@ __device__ __forceinline__ void finish_splits(const WsView& ws, int counter_idx,
         // With a cross-GPU merge and one slot per warp, each thread keeps its merged
         // float4 until every thread is done with the staged partials; the staging
         // area then holds every thread's polled peer words (3 * kMaxPeers uint4).
-        const bool peer_staged = peer != nullptr && nslots <= nwarps &&
+        // (Two ranks poll one round in registers either way; from three on the
+        // register path would need ceil(P / 2) rounds.)
+        const bool peer_staged = peer != nullptr && peer->world > 2 && nslots <= nwarps &&
                                  (size_t)nthreads * 3 * kMaxPeers <= (size_t)stage_vec4;
         float4 keep_r = make_float4(0.f, 0.f, 0.f, 0.f);
         float keep_lse = 0.f;

@@ -79,11 +79,15 @@ def prefetch_target(blocks: Sequence[BlockManifest], query_pos: int, margin: int
 
 
 class _LoadQueue:
-    """Cold-payload loads on one worker thread, keyed by block."""
+    """Cold-payload loads on one worker thread, keyed by block. With
+    ``inline`` set a load runs on the caller's thread when it is submitted
+    (its result waits for the next drain like any finished load): residency
+    decisions then follow one fixed schedule, whatever the thread timing."""
 
     def __init__(self) -> None:
         self._pool = ThreadPoolExecutor(max_workers=1, thread_name_prefix="rfsn-prefetch")
         self._inflight: dict[BlockId, Future] = {}
+        self.inline = False
 
     def __len__(self) -> int:
         return len(self._inflight)
@@ -92,7 +96,15 @@ class _LoadQueue:
         return block_id in self._inflight
 
     def submit(self, block_id: BlockId, load: Callable, manifest: BlockManifest) -> None:
-        self._inflight[block_id] = self._pool.submit(load, manifest)
+        if not self.inline:
+            self._inflight[block_id] = self._pool.submit(load, manifest)
+            return
+        done: Future = Future()
+        try:
+            done.set_result(load(manifest))
+        except Exception as exc:  # noqa: BLE001 - delivered by the drain, as from the worker
+            done.set_exception(exc)
+        self._inflight[block_id] = done
 
     def finished(self) -> Iterator[tuple[BlockId, Future]]:
         """Loads that are done when the walk reaches them, oldest first, each
@@ -123,6 +135,16 @@ class ResidencyManager:
     @property
     def has_pending(self) -> bool:
         return len(self._loads) > 0
+
+    @property
+    def inline_loads(self) -> bool:
+        """Run prefetch loads on the caller's thread when they are scheduled
+        (a deterministic schedule for replays and parity runs); off by default."""
+        return self._loads.inline
+
+    @inline_loads.setter
+    def inline_loads(self, value: bool) -> None:
+        self._loads.inline = bool(value)
 
     def reset(self) -> None:
         self._loads.clear()

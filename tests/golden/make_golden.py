@@ -22,6 +22,12 @@ are:
 * ``rope_golden.npz``     the reference's ``build_rope_tables`` and
   ``_apply_rope`` with tables in the model dtype or another dtype (the RoPE of
   a layer called without tables, or with tables passed in).
+* ``model_slices_golden.npz`` two-layer float32 slices at the head geometry
+  of the Llama-3-8B- and Mistral-7B-shaped configurations (head_dim 128, GQA
+  4, RoPE theta 5e5 / 1e6) with small rings, blocks and warm capacity, so the
+  prompt seals blocks, blocks go cold and decode steps reload them: logits,
+  greedy tokens, layer-0 ring/page-table states and residency counters.
+  Weights are regenerated from the seeds (``slice_weights``).
 * ``tiny_model_golden.npz`` the CPU-runnable tiny model (1 layer, hidden 128,
   2/2 heads, head_dim 64, SwiGLU 4x, vocab 128, tied head, theta 1e4, fp32,
   hot 8 / block 4): prompt of 8 ids (seed 1) + 8 greedy decode steps, with
@@ -325,6 +331,94 @@ def make_tiny_model(mx, out_path: Path) -> None:
         np.savez_compressed(out_path, **blobs)
 
 
+MODEL_SLICES = [
+    # name, seed, config overrides, prompt length, decode steps
+    ("cfg4_slice", 4, dict(rope_base=500000.0, vocab_size=256, hot_capacity=32, block_size_seq=16,
+                           warm_capacity=48, cold_capacity=4096), 96, 12),
+    ("cfg5_slice", 5, dict(rope_base=1e6, vocab_size=320, hot_capacity=64, block_size_seq=32, warm_capacity=64,
+                           cold_capacity=4096), 192, 12),
+]
+SLICE_DIMS = dict(hidden_dim=1024, num_heads=8, num_kv_heads=2, head_dim=128, num_layers=2, ffn_dim=3584,
+                  norm_eps=1e-5, model_dtype="float32")
+
+
+class _InlineExecutor:
+    """Runs a submitted load at once on the caller's thread: a prefetch is
+    complete as soon as it is scheduled, so the residency decisions of a run do
+    not depend on when a worker thread finishes (a deterministic schedule of
+    the reference's policy)."""
+
+    def submit(self, fn, *args):
+        from concurrent.futures import Future
+
+        f = Future()
+        try:
+            f.set_result(fn(*args))
+        except Exception as exc:  # noqa: BLE001 - delivered through the future, as a pool would
+            f.set_exception(exc)
+        return f
+
+
+def slice_weights(param_shapes: dict[str, tuple[int, ...]], seed: int) -> dict[str, np.ndarray]:
+    """normal(0, 0.02) float32 from ``seed`` for every projection/embedding
+    weight in sorted-name order; norm weights keep their initialisation."""
+    rng = np.random.default_rng(seed)
+    return {k: rng.normal(0.0, 0.02, size=param_shapes[k]).astype(np.float32)
+            for k in sorted(param_shapes) if "norm" not in k}
+
+
+def make_model_slices(mx, out_path: Path) -> None:
+    from mlx.utils import tree_flatten, tree_unflatten
+    from rfsn_v10_5.cache import RFSNCache
+    from rfsn_v10_5.config import RFSNConfig, RuntimeMode
+    from rfsn_v10_5.model import RFSNMLX
+
+    blobs: dict[str, np.ndarray] = {}
+    for name, seed, over, n_prompt, n_decode in MODEL_SLICES:
+        with tempfile.TemporaryDirectory() as tmp:
+            cfg = RFSNConfig(**SLICE_DIMS, **over, runtime_mode=RuntimeMode.ARCHIVED, disk_cache_dir=tmp,
+                             session_id=name.replace("_", "-"))
+            model = RFSNMLX(cfg)
+            shapes = {k: tuple(v.shape) for k, v in tree_flatten(model.parameters())}
+            model.update(tree_unflatten([(k, mx.array(v)) for k, v in slice_weights(shapes, seed).items()]))
+            cache = RFSNCache(cfg, batch_size=1)
+            for i in range(cfg.num_layers):  # prefetches complete when scheduled: no timing races
+                cache.layer(i).residency_manager._executor = _InlineExecutor()
+            prompt = np.random.default_rng(seed + 100).integers(0, cfg.vocab_size, size=(1, n_prompt)).astype(np.int32)
+            logits = model.prefill(mx.array(prompt), cache)
+            lc = cache.layer(0)
+            states = []
+
+            def snap():
+                states.append([lc.hot_head_index, lc.hot_seq_len, lc.hot_start] + [
+                    x for m in lc.block_manager.iter_blocks(layer_id=0)
+                    for x in (m.logical_start, m.logical_end, 1 if m.residency.value == "warm_ram" else 0)])
+
+            snap()
+            token = mx.argmax(logits[:, -1, :], axis=-1).astype(mx.int32)
+            tokens = [int(np.array(token)[0])]
+            dec = []
+            pos = n_prompt
+            for _ in range(n_decode):
+                out = model.decode_step(token, cache, pos)
+                dec.append(np.array(out))
+                snap()
+                token = mx.argmax(out, axis=-1).astype(mx.int32)
+                tokens.append(int(np.array(token)[0]))
+                pos += 1
+            metrics = [[cache.layer(i).residency_manager.get_metrics()[k] for k in sorted(
+                cache.layer(i).residency_manager.get_metrics())] for i in range(cfg.num_layers)]
+        width = max(len(x) for x in states)
+        blobs[f"{name}/prompt"] = prompt
+        blobs[f"{name}/prefill_logits"] = np.array(logits)
+        blobs[f"{name}/decode_logits"] = np.stack(dec)
+        blobs[f"{name}/tokens"] = np.array(tokens, np.int32)
+        blobs[f"{name}/ring_states"] = np.array([x + [-1] * (width - len(x)) for x in states], np.int64)
+        blobs[f"{name}/residency_metrics"] = np.array(metrics, np.int64)
+    blobs["__cases__"] = np.array([c[0] for c in MODEL_SLICES])
+    np.savez_compressed(out_path, **blobs)
+
+
 ROPE_CASES = [
     # name, x dtype, table dtype, heads, L, D, start position, base
     ("bf16_tables_bf16", "bfloat16", "bfloat16", 4, 5, 128, 131000, 500000.0),
@@ -371,6 +465,7 @@ def main() -> None:
     make_residency_trace(mx, out / "residency_trace.json")
     make_tiny_model(mx, out / "tiny_model_golden.npz")
     make_rope(mx, out / "rope_golden.npz")
+    make_model_slices(mx, out / "model_slices_golden.npz")
     for p in sorted(out.iterdir()):
         if p.suffix in (".npz", ".json"):
             print(f"{p.name}: {p.stat().st_size} bytes")
