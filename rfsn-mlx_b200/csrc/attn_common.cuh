@@ -154,30 +154,9 @@ __host__ __device__ constexpr int merge_scratch_floats(int nslots, int splits) {
 // merges them in rank order:  out = sum_r e^(lse_r - M) O_r / sum_r e^(lse_r - M).
 // Mailbox halves alternate with the call parity: a rank cannot publish call
 // c + 2 before every peer has published (so finished reading) call c + 1.
-// One source's part, merged into the running (M, W, acc) in rank order.
-__device__ __forceinline__ void merge_peer_part(float ls, float4 v, float& M, float& W, float4& acc) {
-    if (ls == -CUDART_INF_F) return;  // a part that saw no visible key
-    if (ls > M) {
-        const float sc = (M == -CUDART_INF_F) ? 0.f : expf(M - ls);
-        W = W * sc + 1.f;
-        acc = make_float4(acc.x * sc + v.x, acc.y * sc + v.y, acc.z * sc + v.z, acc.w * sc + v.w);
-        M = ls;
-    } else {
-        const float wgt = expf(ls - M);
-        W += wgt;
-        acc = make_float4(acc.x + wgt * v.x, acc.y + wgt * v.y, acc.z + wgt * v.z, acc.w + wgt * v.w);
-    }
-}
-
-// `stage` (optional): this thread's shared-memory scratch of 3 * kMaxPeers
-// uint4. With it, every source's words are fetched in one round
-// (cp.async from L2, where the peers' NVLink stores land) and checked there,
-// so a poll costs one round trip whatever the number of ranks; without it the
-// words are polled into registers two sources at a time.
 __device__ __forceinline__ void peer_store_and_merge(const PeerParams& peer, const WsView& ws, int call, int group,
                                                      int sl, int d4, int head_dim, float4 r, float my_lse,
-                                                     const OutMap& om, float* out, float* lse,
-                                                     uint4* stage = nullptr) {
+                                                     const OutMap& om, float* out, float* lse) {
     if (*reinterpret_cast<volatile const int*>(peer.poison) != 0) {
         // An earlier call of this group gave up waiting for a peer: the ranks'
         // call stamps may no longer agree, so words carrying this call's stamp
@@ -201,49 +180,16 @@ __device__ __forceinline__ void peer_store_and_merge(const PeerParams& peer, con
     }
     const uint2* local = peer.words[peer.rank] + (size_t)(call & 1) * half + ((size_t)group * kPeerSlots + sl) * slot_words;
     const size_t src_stride = (size_t)groups * kPeerSlots * slot_words;
+    // Sources are polled two at a time: the words of a group are requested
+    // together (one round trip per poll instead of one per rank), and the
+    // sources that have not arrived are polled again. Merged in rank order.
+    constexpr int kGroup = 2;  // the load results of a group stay in registers (no spill at 2 CTAs per SM)
     const long long t0 = global_ns();
     bool timed_out = false;
     // online merge in rank order: running max M, weight sum W, weighted sum acc
     float M = -CUDART_INF_F, W = 0.f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (stage != nullptr) {
-        const unsigned want = (1u << P) - 1u;
-        unsigned ready = 0;
-        for (;;) {
-            for (int s = 0; s < P; ++s) {
-                if ((ready >> s) & 1u) continue;
-                const uint2* w = local + s * src_stride;
-                cp_async_16(stage + 3 * s, w + 4 * d4);
-                cp_async_16(stage + 3 * s + 1, w + 4 * d4 + 2);
-                cp_async_16(stage + 3 * s + 2, w + head_dim);
-            }
-            cp_async_commit();
-            cp_async_wait_all();
-            for (int s = 0; s < P; ++s) {
-                if ((ready >> s) & 1u) continue;
-                const uint4 a = stage[3 * s], b = stage[3 * s + 1], l = stage[3 * s + 2];
-                if (a.y == stamp && a.w == stamp && b.y == stamp && b.w == stamp && l.y == stamp) ready |= 1u << s;
-            }
-            if (ready == want) break;
-            if (global_ns() - t0 > peer.timeout_ns) {
-                timed_out = true;
-                break;
-            }
-            __nanosleep(20);
-        }
-        for (int s = 0; s < P; ++s) {
-            if (!((ready >> s) & 1u)) continue;  // after a timeout only the parts that arrived
-            const uint4 a = stage[3 * s], b = stage[3 * s + 1], l = stage[3 * s + 2];
-            merge_peer_part(__uint_as_float(l.x),
-                            make_float4(__uint_as_float(a.x), __uint_as_float(a.z), __uint_as_float(b.x),
-                                        __uint_as_float(b.z)),
-                            M, W, acc);
-        }
-    }
-    // Without a staging area sources are polled two at a time: the words of a
-    // pair are requested together and the load results stay in registers.
-    constexpr int kGroup = 2;
-    for (int g0 = 0; stage == nullptr && g0 < P && !timed_out; g0 += kGroup) {
+    for (int g0 = 0; g0 < P && !timed_out; g0 += kGroup) {
         const int n = min(kGroup, P - g0);
         const unsigned want = (1u << n) - 1u;
         unsigned ready = 0;
@@ -276,10 +222,20 @@ __device__ __forceinline__ void peer_store_and_merge(const PeerParams& peer, con
 #pragma unroll
         for (int s = 0; s < kGroup; ++s) {
             if (s >= n || !((ready >> s) & 1u)) continue;  // after a timeout only the parts that arrived
-            merge_peer_part(__uint_as_float(l[s].x),
-                            make_float4(__uint_as_float(a[s].x), __uint_as_float(a[s].z), __uint_as_float(b[s].x),
-                                        __uint_as_float(b[s].z)),
-                            M, W, acc);
+            const float ls = __uint_as_float(l[s].x);
+            if (ls == -CUDART_INF_F) continue;  // a part that saw no visible key
+            const float4 v = make_float4(__uint_as_float(a[s].x), __uint_as_float(a[s].z), __uint_as_float(b[s].x),
+                                         __uint_as_float(b[s].z));
+            if (ls > M) {
+                const float sc = (M == -CUDART_INF_F) ? 0.f : expf(M - ls);
+                W = W * sc + 1.f;
+                acc = make_float4(acc.x * sc + v.x, acc.y * sc + v.y, acc.z * sc + v.z, acc.w * sc + v.w);
+                M = ls;
+            } else {
+                const float wgt = expf(ls - M);
+                W += wgt;
+                acc = make_float4(acc.x + wgt * v.x, acc.y + wgt * v.y, acc.z + wgt * v.z, acc.w + wgt * v.w);
+            }
         }
     }
     if (timed_out) {
@@ -359,16 +315,6 @@ __device__ __forceinline__ void finish_splits(const WsView& ws, int counter_idx,
         const uint32_t a_m = smem_u32(st_m), a_l = smem_u32(st_l), a_o = smem_u32(stage);
         const uint32_t ml_step = 4u * split_stride, o_step = 16u * items;
         constexpr int kB = 8;  // splits per batch: independent loads issued together
-        // With a cross-GPU merge and one slot per warp, each thread keeps its merged
-        // float4 until every thread is done with the staged partials; the staging
-        // area then holds every thread's polled peer words (3 * kMaxPeers uint4).
-        // (Two ranks poll one round in registers either way; from three on the
-        // register path would need ceil(P / 2) rounds.)
-        const bool peer_staged = peer != nullptr && peer->world > 2 && nslots <= nwarps &&
-                                 (size_t)nthreads * 3 * kMaxPeers <= (size_t)stage_vec4;
-        float4 keep_r = make_float4(0.f, 0.f, 0.f, 0.f);
-        float keep_lse = 0.f;
-        int keep_sl = -1;
         for (int sl = warp; sl < nslots; sl += nwarps) {
             const int d4 = lane, idx = sl * d4n + d4;
             const uint32_t am = a_m + 4u * (slot0 + sl), al = a_l + 4u * (slot0 + sl), ao = a_o + 16u * idx;
@@ -409,19 +355,8 @@ __device__ __forceinline__ void finish_splits(const WsView& ws, int counter_idx,
             if (peer == nullptr) {
                 *reinterpret_cast<float4*>(out + om.row(bh, slot0 + sl) * head_dim + 4 * d4) = r;
                 if (lse != nullptr && d4 == 0) lse[om.row(bh, slot0 + sl)] = my_lse;
-            } else if (peer_staged) {
-                keep_r = r;
-                keep_lse = my_lse;
-                keep_sl = sl;
             } else {
                 peer_store_and_merge(*peer, ws, call, bh, sl, d4, head_dim, r, my_lse, om, out, lse);
-            }
-        }
-        if (peer_staged) {
-            named_barrier_sync(bar_id, nthreads);  // the staged partials are no longer read
-            if (keep_sl >= 0) {
-                peer_store_and_merge(*peer, ws, call, bh, keep_sl, lane, head_dim, keep_r, keep_lse, om, out, lse,
-                                     reinterpret_cast<uint4*>(stage) + (size_t)tid * 3 * kMaxPeers);
             }
         }
         if (splits > 1 && tid == 0) ws.counters[counter_idx] = 0;

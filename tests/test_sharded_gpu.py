@@ -175,14 +175,25 @@ def _nccl_worker(rank, world, port, results, mode="nccl"):
         results.put((rank, "crash: " + traceback.format_exc()))
 
 
-@pytest.mark.skipif("not __import__('torch').cuda.device_count() >= 2", reason="needs 2 GPUs")
+def _gpus():
+    import torch
+
+    return torch.cuda.device_count()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("mode", ["nccl", "p2p"])
-def test_sharded_decode_step_two_gpus(mode):
+def test_sharded_decode_step_on_gpus(mode, world):
+    """One process per GPU (2, 4 or 8 of them, skipped when fewer are
+    visible): the merged result of every rank equals the unsharded oracle, for
+    the NCCL gather and for the merge fused into the kernel over NVLink (from
+    three ranks on, every peer's words are polled in one round)."""
     import torch
 
     from oracle.rope import apply_rope, rope_tables
 
-    world = 2
+    if _gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     results = ctx.Queue()
     port = _port()
