@@ -727,6 +727,33 @@ def run_ours(args, w):
     return 0
 
 
+def run_shard(args, w):
+    """``--shard-of N``: one rank's share of the N-way partition of the
+    workload (rank 0's archived blocks) on one GPU, the decode kernel alone,
+    the shard rotated with copies of itself so every call reads HBM. Used to
+    profile the per-rank kernel of a sharded run on one GPU."""
+    import torch
+
+    torch.cuda.set_device(0)
+    device = torch.device("cuda", 0)
+    n = args.shard_of
+    cache, _, local_tokens, total_tokens = build_shard(w, 0, n, device, 0)
+    caches = [cache] + [build_shard(w, 0, n, device, 0)[0] for _ in range(shard_copies(w, n, total_tokens) - 1)]
+    ms, launches = device_throughput(caches, w, 1, args.steps, args.warmup, args.calls_per_step, collective=False)
+    calls = args.steps * args.calls_per_step
+    us = ms * 1e3 / calls
+    nbytes = algorithmic_bytes(w, local_tokens)
+    peak, kind = measured_peaks()
+    print(json.dumps({
+        "metric": "decode-attention kernel time of one rank's shard (us/call)", "workload": args.workload,
+        "shard": f"rank 0 of {n}", "shard_tokens": local_tokens, "shard_copies": len(caches), "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": False, "value": us, "unit": "us/call",
+        "gbs": nbytes / us / 1e3, "frac_of_measured_hbm": nbytes / us / 1e3 / peak, "peak_kind": kind,
+        "gpu_launches": launches,
+    }), flush=True)
+    return 0
+
+
 def secondary_8k(args, device, peak):
     """The 8K fp16 workload at N = 1, rotating 8 copies of the context so that
     consecutive calls miss L2 (8 x 33.6 MB > 126 MB)."""
@@ -1177,6 +1204,8 @@ def main() -> int:
     ap.add_argument("--no-prefill", action="store_true", help="skip the chunked-prefill measurement (N = 1)")
     ap.add_argument("--decode-steps", type=int, default=None,
                     help="greedy decode steps of the model7b workload (default 128)")
+    ap.add_argument("--shard-of", type=int, default=0,
+                    help="time rank 0's shard of an N-way partition alone on one GPU (kernel only)")
     ap.add_argument("--merge", choices=["p2p", "nccl"], default="p2p",
                     help="cross-GPU merge for N > 1: fused NVLink mailboxes (default) or NCCL all-gather")
     args = ap.parse_args()
@@ -1193,6 +1222,8 @@ def main() -> int:
     w = WORKLOADS[args.workload]
     if args.impl == "reference":
         return run_reference(args, w)
+    if args.shard_of > 1:
+        return run_shard(args, w)
     return run_ours(args, w)
 
 
