@@ -87,3 +87,44 @@ def test_reference_arm_prints_one_contract_line_on_host_cores():
 def test_reference_arm_runs_on_rank_zero_only():
     assert _run_bench(["--impl", "reference", "--workload", "decode8k_fp16", "--steps", "1", "--warmup", "0"],
                       {"RANK": "1", "LOCAL_RANK": "1", "WORLD_SIZE": "2"}) == []
+
+
+def test_shard_rotation_keeps_every_call_out_of_l2():
+    """At N > 1 every rank rotates enough copies of its shard that the copies
+    together exceed twice the 126 MB L2 (the same count on every rank); one
+    GPU reads the whole context and needs none."""
+    import importlib.util
+    from pathlib import Path
+
+    spec = importlib.util.spec_from_file_location("bench_mod", Path(__file__).resolve().parent.parent / "bench.py")
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    w = bench.WORKLOADS["decode128k_bf16"]
+    total = sum(w["blocks"]) + w["hot"]
+    assert bench.shard_copies(w, 1, total) == 1
+    for world in (2, 4, 8):
+        copies = bench.shard_copies(w, world, total)
+        per_rank = bench.algorithmic_bytes(w, total) / world
+        assert copies * per_rank >= bench.L2_ROTATION_BYTES >= 2 * 126e6
+        assert (copies - 1) * per_rank < bench.L2_ROTATION_BYTES
+    assert [bench.shard_copies(w, n, total) for n in (2, 4, 8)] == [1, 2, 4]
+
+
+def test_cpu_baseline_work_items_cover_every_head_and_segment_once():
+    """The CPU baseline's work items: each KV head's segments in consecutive
+    runs, every (head, segment) exactly once, at least two items per worker
+    where the segments allow it; the combined result equals one evaluation."""
+    import numpy as np
+
+    from oracle.cpu_baseline import attention_all_cores, synthetic_decode_inputs, work_items
+    from oracle.segmented_attention import run_segmented_attention
+
+    for heads, segs, threads in ((8, 129, 16), (8, 25, 32), (2, 3, 8), (8, 1, 4)):
+        items = work_items(heads, segs, threads)
+        seen = sorted((h, s) for h, a, b in items for s in range(a, b))
+        assert seen == [(h, s) for h in range(heads) for s in range(segs)]
+        assert len(items) >= min(2 * threads, heads * segs)
+    q, seg_list, qpos = synthetic_decode_inputs([40] * 6 + [9], 30, 2, 8, 16, "float16", 5)
+    out, workers = attention_all_cores(q, seg_list, qpos, 4)
+    ref = run_segmented_attention(q, seg_list, qpos)
+    assert workers == 4 and float(np.abs(out - ref).max()) <= 2e-6
