@@ -6,8 +6,8 @@ The reference's test modules (``rfsn_v10_5`` package tests) import
 here those names resolve to this repository's drop-in modules, while the
 reference's own ``config``, ``layer``, ``model`` and ``attention_exact`` run
 unmodified over the torch-CPU ``mlx`` shim. So the reference's model drives
-the drop-in cache exactly as it drives its own, and the reference's
-assertions judge the result.
+the drop-in cache exactly as it drives its own, and the reference's own
+assertions check the result.
 
 Two adapters sit on the boundary, because the drop-in takes torch tensors
 where the reference passes MLX arrays:
