@@ -32,6 +32,9 @@ At N = 1 the line also carries ``secondary`` (the 8K fp16 decode workload)
 and ``prefill``: one layer of a 32K-token prompt prefilled in 2048-token
 chunks on the tcgen05 tensor-core kernel, against the measured bf16 peak.
 
+``--shard-of N`` times rank 0's shard of the N-way partition alone on one GPU
+(the per-rank kernel of a sharded run, for profiling).
+
 Other workloads (one GPU, one JSON line each): ``prefill32k_chunk2048_bf16``,
 ``warm_reload_bf16`` (decode steps that reload cold blocks), and the whole
 models ``model8b_e2e_bf16`` (Llama-3-8B shape) and
