@@ -778,6 +778,8 @@ class LayerKVCache:
         cos_t = sin_t = None
         table_dtype = self.dtype
         if rope_tables is not None:
+            if not isinstance(rope_tables, (tuple, list)) or len(rope_tables) != 2:
+                raise ValueError("rope_tables must be a (cos, sin) pair of tensors")
             cos_t, sin_t = rope_tables
             if not (isinstance(cos_t, torch.Tensor) and isinstance(sin_t, torch.Tensor)):
                 raise ValueError("rope_tables must be a (cos, sin) pair of tensors")

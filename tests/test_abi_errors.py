@@ -52,6 +52,16 @@ def test_ring_and_block_copy_arguments(lib):
                                           None), "NULL step state")
     _expect_bad(lib.rfsn_rope_append_step(FAKE, FAKE, FAKE, f32, FAKE, FAKE, None, 1, 32, 8, 1, 128, FAKE, None, 0, 64,
                                           None), "NULL arena")
+    # (q, k, v, dtype, cos, sin, table dtype, inv_freq, pos0, batch, heads, kv heads, len, d, q_out, arena,
+    #  row0, capacity, write index, stream)
+    _expect_bad(lib.rfsn_rope_append_tables(FAKE, FAKE, FAKE, f32, FAKE, FAKE, f32, FAKE, 0, 1, 32, 8, 1, 128, FAKE,
+                                            None, 0, 64, 0, None), "NULL arena")
+    _expect_bad(lib.rfsn_rope_append_tables(FAKE, FAKE, FAKE, f32, FAKE, None, f32, FAKE, 0, 1, 32, 8, 1, 128, FAKE,
+                                            FAKE, 0, 64, 0, None), "go together")
+    _expect_bad(lib.rfsn_rope_append_tables(FAKE, FAKE, FAKE, f32, None, None, f32, None, 0, 1, 32, 8, 1, 128, FAKE,
+                                            FAKE, 0, 64, 0, None), "no tables and no inv_freq")
+    _expect_bad(lib.rfsn_rope_append_tables(FAKE, None, FAKE, f32, FAKE, FAKE, f32, FAKE, 0, 1, 32, 8, 1, 128, FAKE,
+                                            FAKE, 0, 64, 0, None), "NULL q/k/v/q_out")
     _expect_bad(lib.rfsn_arena_copy_rows(None, 0, 0, 0, 0, 1, None), "NULL arena")
     _expect_bad(lib.rfsn_block_upload(None, 0, 1, FAKE, FAKE, None, None), "NULL arena")
     _expect_bad(lib.rfsn_block_download(None, 0, 1, FAKE, FAKE, None, None), "NULL arena")

@@ -425,3 +425,26 @@ def test_rope_frequency_table_matches_oracle_on_host(tmp_path, head_dim, base):
     c = LayerKVCache(cfg, 1, 2, 1, session_id="r", ops=FakeDeviceOps())
     table = c.inv_freq().numpy()
     assert table.dtype == np.float32 and np.array_equal(table, inv_freq(head_dim, base))
+
+
+def test_rope_tables_are_checked_before_any_device_work(tmp_path):
+    """``append_rope_tables`` (a layer called with ``rope_tables``) rejects
+    tables that are not a (cos, sin) pair of float tensors of one row per new
+    position, with ValueError as the reference's shape errors, before the ring
+    or the device is touched."""
+    import torch
+
+    from cache_replay import _config
+    from rfsn_b200.cache import LayerKVCache
+
+    cache = LayerKVCache(_config(8, 4, "archived", 64, str(tmp_path)), 1, 2, 1, session_id="s", ops=FakeDeviceOps(),
+                         device="cpu")
+    q = torch.zeros((1, 2, 3, 4))
+    k = v = torch.zeros((1, 1, 3, 4))
+    good = torch.zeros((3, 4))
+    for tables, msg in (((good,), "pair"), ((good, "x"), "pair"), ((good.int(), good.int()), "float dtype"),
+                        ((good, good.half()), "float dtype"), ((torch.zeros((2, 4)), torch.zeros((2, 4))), "[3, 4]"),
+                        ((torch.zeros((3, 8)), torch.zeros((3, 8))), "[3, 4]")):
+        with pytest.raises(ValueError, match=msg.replace("[", r"\[").replace("]", r"\]")):
+            cache.append_rope_tables(q, k, v, 0, tables)
+    assert cache.hot_seq_len == 0 and not cache._ops.calls
