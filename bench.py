@@ -821,9 +821,12 @@ def bf16_peak() -> tuple[float, str]:
 
 def prefill_32k(args, device):
     """Chunked-prefill attention on the tcgen05 kernel: the 16 chunk calls of one
-    layer, K/V resident in HBM, timed with CUDA events. Useful FLOPs count the
-    causal products once (4 * heads * head_dim per query-key pair); the kernel
-    issues twice that on the tensor cores (16-bit high + residual parts of q and P)."""
+    layer, K/V resident in HBM, timed with CUDA events. q holds bf16 values, as
+    the projection and RoPE of a bf16 model deliver it; the same layer with
+    float32 q (random values with residuals) is timed too. Useful FLOPs count
+    the causal products once (4 * heads * head_dim per query-key pair); the
+    kernel issues 1.5x that on the tensor cores for 16-bit q (q K^T, and the
+    16-bit high + residual parts of P in P V) and 2x for float32 q."""
     import ctypes
 
     import torch
@@ -836,7 +839,8 @@ def prefill_32k(args, device):
     gen = torch.Generator(device=device).manual_seed(5)
     k = torch.randn((Hkv, rows, D), generator=gen, device=device).to(torch.bfloat16)
     v = torch.randn((Hkv, rows, D), generator=gen, device=device).to(torch.bfloat16)
-    q = torch.randn((1, H, chunk, D), generator=gen, device=device)
+    q32 = torch.randn((1, H, chunk, D), generator=gen, device=device)
+    q = q32.to(torch.bfloat16).float()
     out = torch.empty_like(q)
     lse = torch.empty((1, H, chunk), device=device)
     arena = native.Arena(k, v)
@@ -859,24 +863,29 @@ def prefill_32k(args, device):
         flops += 4.0 * H * D * (chunk * c * chunk + chunk * (chunk + 1) / 2)
     lib = native.lib()
 
-    def run_layer():
+    def run_layer(qt):
         for table, hot, pos in calls:
-            native.check(lib.rfsn_paged_attention(arena.handle, q.data_ptr(), 1, H, Hkv, chunk, pos, ctypes.byref(table),
+            native.check(lib.rfsn_paged_attention(arena.handle, qt.data_ptr(), 1, H, Hkv, chunk, pos, ctypes.byref(table),
                                                   ctypes.byref(hot), out.data_ptr(), lse.data_ptr(), ws.data_ptr(),
                                                   nbytes, 0, native.stream_ptr()), "prefill")
 
-    for _ in range(2):
-        run_layer()
-    torch.cuda.synchronize()
     reps = max(3, min(args.steps, 10))
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record()
-    for _ in range(reps):
-        run_layer()
-    end.record()
-    end.synchronize()
-    native.check(lib.rfsn_workspace_check(ws.data_ptr(), native.stream_ptr(), 30_000_000), "prefill workspace")
-    ms = start.elapsed_time(end) / reps
+
+    def time_layer(qt):
+        for _ in range(2):
+            run_layer(qt)
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(reps):
+            run_layer(qt)
+        end.record()
+        end.synchronize()
+        native.check(lib.rfsn_workspace_check(ws.data_ptr(), native.stream_ptr(), 30_000_000), "prefill workspace")
+        return start.elapsed_time(end) / reps
+
+    ms_fp32_q = time_layer(q32)
+    ms = time_layer(q)  # last: `out` holds the 16-bit q layer's last chunk
     # correctness of the last chunk (its output is what `out` holds now): the first
     # and last query row of every (query block, KV head) unit against a dense
     # float64 softmax over the keys in logical order (archived blocks, then the ring)
@@ -910,9 +919,12 @@ def prefill_32k(args, device):
             "unit": "TFLOP/s",
             "frac": tflops / peak,
             "peak_kind": kind,
-            "tensor_work_factor": 2,
+            "tensor_work_factor": 1.5,
             "kernel": "rfsn::prefill::prefill_attn_kernel (tcgen05, TMEM accumulators)",
         },
+        "q": "bf16 values (a bf16 model's projection + RoPE output), passed as float32",
+        "float32_q": {"ms_per_layer": ms_fp32_q, "tflops_useful": flops / (ms_fp32_q / 1e3) / 1e12,
+                      "frac": flops / (ms_fp32_q / 1e3) / 1e12 / peak, "tensor_work_factor": 2},
         "l2": "K/V 67 MB + q/out per call; every chunk streams its whole causal context",
         "parity": parity,
     }

@@ -9,11 +9,15 @@
 // (kv_head * G + r % G) at chunk position (base + r / G), so every K/V tile
 // staged in shared memory serves all G query heads of its KV head.
 //
-// float32 accuracy: q (pre-scaled by log2(e)/sqrt(d)) and the probabilities
-// P are each split into a 16-bit high part and a 16-bit residual
-// (x = hi + lo to ~16 significand bits); S = Qhi K^T + Qlo K^T and
-// O += Phi V + Plo V, all accumulated in float32 in TMEM. K and V are stored
-// in 16 bits already, so they enter the products exactly.
+// float32 accuracy: q and the probabilities P are each split into a 16-bit
+// high part and a 16-bit residual (x = hi + lo to ~16 significand bits);
+// S = Qhi K^T + Qlo K^T and O += Phi V + Plo V, all accumulated in float32 in
+// TMEM, and the softmax scales S by log2(e)/sqrt(d) in float32. K and V are
+// stored in 16 bits already, so they enter the products exactly. When every q
+// element of the CTA is a 16-bit value (the q of a bf16/fp16 model: projection
+// and RoPE round to the model dtype) all residuals are zero and the Qlo K^T
+// product, which would add exact zeros, is not issued: 3 products per tile
+// instead of 4.
 //
 // Warps:
 //   0-7  softmax: warp w owns TMEM lane quarter w % 4 (32 rows, thread = row)
@@ -86,6 +90,7 @@ struct Smem {
     uint32_t tmem;
     int abort;
     int flag;  // this CTA merges the key-range splits of its query block
+    int q_lo;  // some q element of the CTA has a nonzero 16-bit residual
 };
 
 // (a, b) -> packed 16-bit high parts and packed 16-bit residuals (a = hi + lo to
@@ -257,6 +262,7 @@ prefill_attn_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
             mbar_init(&sm.pair_l[qd], 64);
         }
         sm.abort = 0;
+        sm.q_lo = 0;
         fence_mbar_init();
     }
     if (warp == MMA_WARP) {
@@ -355,6 +361,7 @@ prefill_attn_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
             const uint32_t id_qk = tc::idesc_f16(kBf16, false, false, BM, BN);
             const uint32_t id_pv = tc::idesc_f16(kBf16, false, true, BM, D);
             const uint32_t tO = tmem + COL_O;
+            const int q_parts = sm.q_lo ? 2 : 1;  // written before barrier 1
             bool pending = false;  // tensor-core work issued whose completion is not yet observed
             // t: tile whose S is issued this round; it = t - 1: tile whose PV follows
             for (int t = 0;; ++t) {
@@ -374,10 +381,10 @@ prefill_attn_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
                         break;
                     }
                     tc::fence_after_sync();
-                    // S(t) = Qhi K^T + Qlo K^T
+                    // S(t) = Qhi K^T (+ Qlo K^T when q has residuals)
                     const uint32_t tS = tmem + 128 * (t % NSB);
 #pragma unroll 1
-                    for (int part = 0; part < 2; ++part) {
+                    for (int part = 0; part < q_parts; ++part) {
                         const uint32_t tQ = tmem + (part ? COL_QLO : COL_QHI);
 #pragma unroll
                         for (int kk = 0; kk < 8; ++kk) {
@@ -433,14 +440,19 @@ prefill_attn_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
             const int qrow = pos_base + j;
             const bool ok_row = j < ppc && qrow < p.q_len;
             const float* src = p.q + (((size_t)b * p.q_heads + hk * G + g) * p.q_len + (ok_row ? qrow : 0)) * D + 64 * ch;
-            uint32_t hi[32], lo[32];
+            uint32_t hi[32], lo[32], any_lo = 0;
 #pragma unroll
             for (int c = 0; c < 16; ++c) {  // 16 chunks of 4 elements
                 float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
                 if (ok_row) a = *reinterpret_cast<const float4*>(src + 4 * c);
-                split2<T>(a.x * p.qscale, a.y * p.qscale, hi[2 * c], lo[2 * c]);
-                split2<T>(a.z * p.qscale, a.w * p.qscale, hi[2 * c + 1], lo[2 * c + 1]);
+                split2<T>(a.x, a.y, hi[2 * c], lo[2 * c]);
+                split2<T>(a.z, a.w, hi[2 * c + 1], lo[2 * c + 1]);
+                any_lo |= lo[2 * c] | lo[2 * c + 1];
             }
+            // a residual of 16 zero bits contributes nothing to S: the Qlo product is
+            // needed only if some residual of the CTA is nonzero (same value from every
+            // writer; barrier 1 orders it before the MMA issuer reads it)
+            if (__any_sync(0xffffffffu, any_lo != 0) && lane == 0) sm.q_lo = 1;
             const uint32_t lane_q = (uint32_t)(32 * qd) << 16;
             tc::st_32x32b_x32(tmem + lane_q + COL_QHI + 32 * ch, hi);
             tc::st_32x32b_x32(tmem + lane_q + COL_QLO + 32 * ch, lo);
@@ -483,7 +495,9 @@ prefill_attn_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
                     mx[c & 3] = fmaxf(mx[c & 3], x);
                 }
             }
-            float tmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+            // S holds q.k unscaled; maxima and probabilities are in units of
+            // log2(e)/sqrt(d) (qscale > 0, so the maximum commutes with the scale)
+            float tmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * p.qscale;
             // row maximum over both key halves
             sm.red[it & 1][ch][r] = tmax;
             mbar_arrive(&sm.pair[qd][it & 1]);
@@ -511,8 +525,8 @@ prefill_attn_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
             uint32_t hi[32], lo[32];
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
-                const float p0 = tc::ex2(__uint_as_float(sr[2 * e]) - ms);
-                const float p1 = tc::ex2(__uint_as_float(sr[2 * e + 1]) - ms);
+                const float p0 = tc::ex2(fmaf(__uint_as_float(sr[2 * e]), p.qscale, -ms));
+                const float p1 = tc::ex2(fmaf(__uint_as_float(sr[2 * e + 1]), p.qscale, -ms));
                 rs[e & 3] += p0 + p1;
                 split2<T>(p0, p1, hi[e], lo[e]);
             }

@@ -216,6 +216,53 @@ def test_tensor_core_prefill_key_range_splits(dtype, q_len, blocks, hot):
     _check(lay, q, lay.total_tokens - q_len)
 
 
+def _round_q(q, dtype):
+    """q rounded to the model dtype, as a bf16/fp16 model's projection and RoPE
+    deliver it (float32 storage of 16-bit values)."""
+    import torch
+
+    return torch.from_numpy(q).to(getattr(torch, dtype)).float().numpy()
+
+
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
+@pytest.mark.parametrize("q_len,G,blocks,ring,hot,head", [
+    (128, 4, [256] * 6, 2048, 2048, 512),          # wrapped full ring
+    (200, 2, [1000, 333, 77], 512, 400, 300),      # ragged chunk, odd span lengths
+    (1280, 4, [1000] * 5, 1024, 1024, 7),          # key-range splits
+])
+def test_tensor_core_prefill_16bit_q(dtype, q_len, G, blocks, ring, hot, head):
+    # every q element is a 16-bit value: the kernel skips the q residual product
+    # (all residuals are zero) and must give the same float32-level result
+    Hkv = 4
+    lay = make_layout(dtype, 1, Hkv, 128, blocks, ring, hot, head, seed=86)
+    q = _round_q(_q(86, 1, Hkv * G, q_len, 128), dtype)
+    _check(lay, q, lay.total_tokens - q_len)
+
+
+def test_tensor_core_prefill_16bit_q_except_one_row():
+    # one query row (head 5, position 300) keeps float32 values with residuals: its
+    # CTA issues the residual product and the other CTAs do not; the oracle
+    # separates the two outcomes for that row by far more than the guard
+    lay = make_layout("bfloat16", 1, 4, 128, [512] * 4, 1024, 1024, 0, seed=87)
+    q32 = _q(87, 1, 16, 512, 128)
+    q = _round_q(q32, "bfloat16")
+    q[0, 5, 300] = 4.0 * q32[0, 5, 300]
+    q_pos0 = lay.total_tokens - 512
+    ref = run_segmented_attention(q, lay.oracle_segments(), q_pos0, grouped=True)
+    ref16 = run_segmented_attention(_round_q(q, "bfloat16"), lay.oracle_segments(), q_pos0, grouped=True)
+    assert float(np.abs(ref - ref16)[0, 5, 300].max()) > 20 * GUARD
+    _check(lay, q, q_pos0)
+
+
+def test_tensor_core_prefill_peaky_scores_16bit_q():
+    # large, concentrated scores with 16-bit q: S = q.k is exact in float32 and
+    # the scale is applied in float32, so the float32 guard still holds
+    lay = make_layout("bfloat16", 1, 2, 128, [256, 256], 256, 200, 0, seed=88)
+    rng = np.random.default_rng(88)
+    q = _round_q((rng.standard_normal((1, 8, 128, 128)) * 6.0).astype(np.float32), "bfloat16")
+    _check(lay, q, lay.total_tokens - 128)
+
+
 def _prefill_32k_last_chunk(make_q, seed):
     """The last 2,048-token chunk (positions 30,720-32,767) of a 32,768-token
     prompt over 14 archived blocks of 2,048 plus the full 4,096-token ring,
@@ -248,6 +295,12 @@ def _prefill_32k_last_chunk(make_q, seed):
 def test_tensor_core_prefill_32k_prompt_last_chunk_sampled_rows():
     """The chunk geometry of the 32K-prompt prefill workload with N(0, 1) data."""
     err = _prefill_32k_last_chunk(lambda lay: _q(1085, 1, 32, 2048, 128), seed=85)
+    assert err <= ATOL and err <= GUARD, err
+
+
+def test_tensor_core_prefill_32k_prompt_last_chunk_16bit_q():
+    """The same geometry with the q a bf16 model delivers (16-bit values)."""
+    err = _prefill_32k_last_chunk(lambda lay: _round_q(_q(1089, 1, 32, 2048, 128), "bfloat16"), seed=89)
     assert err <= ATOL and err <= GUARD, err
 
 
