@@ -87,17 +87,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+__device__ __forceinline__ long long global_ns() {
+    long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
 // Bounded wait on an mbarrier phase. try_wait suspends the thread for a
-// hardware-defined interval per attempt, so the limit is a few seconds at most.
-// Gives up early (returns false) once *abort_flag (if given) becomes non-zero.
-constexpr uint32_t kWaitLimit = 1u << 24;
+// hardware-defined interval per attempt (long enough that a count of attempts
+// is no bound on the time), so the limit is taken on the global timer: the
+// wait gives up (returns false) after kWaitNs, or early once *abort_flag (if
+// given) becomes non-zero.
+constexpr long long kWaitNs = 2000000000LL;
 
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, const int* abort_flag) {
-    for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = global_ns();
+    for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (abort_flag != nullptr && (i & 1023u) == 1023u && *(volatile const int*)abort_flag) return false;
+        if ((i & 15u) == 0) {
+            if (abort_flag != nullptr && *(volatile const int*)abort_flag) return false;
+            if (global_ns() - t0 > kWaitNs) return false;
+        }
     }
-    return false;
 }
 
 // TMA: 2-D tiled bulk tensor load global -> shared, completion on an mbarrier.
@@ -338,12 +350,6 @@ __device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
     int old;
     asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
     return old;
-}
-
-__device__ __forceinline__ long long global_ns() {
-    long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
 }
 
 // Output addressing: slot j of kv group (b, hk) is query row r = j / G of q

@@ -8,7 +8,7 @@ q and p, so a tighter 1e-4 guard is also asserted to catch precision loss.
 import numpy as np
 import pytest
 
-from _util import golden_attention_cases, make_layout, run_paged
+from _util import from_storage, golden_attention_cases, make_layout, run_paged, to_storage
 from oracle.segmented_attention import merge_partials, run_segmented_attention
 
 pytestmark = pytest.mark.gpu
@@ -261,6 +261,34 @@ def test_tensor_core_prefill_peaky_scores_16bit_q():
     rng = np.random.default_rng(88)
     q = _round_q((rng.standard_normal((1, 8, 128, 128)) * 6.0).astype(np.float32), "bfloat16")
     _check(lay, q, lay.total_tokens - 128)
+
+
+def _scale_block_keys(lay, block, factor):
+    """Multiply the K rows of one archived block by ``factor`` (in the storage dtype)."""
+    kf = from_storage(lay.k_store, lay.dtype)
+    row, _, n, _ = lay.records[block]
+    kf[:, row:row + n] *= np.float32(factor)
+    lay.k_store = to_storage(kf, lay.dtype)
+
+
+@pytest.mark.parametrize("dtype,scales", [("bfloat16", (16.0, 64.0)), ("float16", (4.0, 12.0))])
+def test_tensor_core_prefill_reference_maximum_moves(dtype, scales):
+    # blocks 1 and 2 score far above block 0, twice (row maxima of ~4, ~60 and ~230
+    # in log2 units for bf16): each row's reference maximum moves twice and the
+    # accumulated O and row sums are rescaled. q holds 16-bit values, so the scores
+    # are exact products (with float32 q, scores of ~200 nats would carry the q
+    # split's ~2^-17 relative error into the output at the 1e-4 level)
+    lay = make_layout(dtype, 1, 2, 128, [256, 256, 256], 512, 300, 0, seed=90, shuffle=False, gap=0)
+    _scale_block_keys(lay, 1, scales[0])
+    _scale_block_keys(lay, 2, scales[1])
+    _check(lay, _round_q(_q(90, 1, 8, 128, 128), dtype), lay.total_tokens - 128)
+
+
+def test_tensor_core_prefill_reference_maximum_moves_with_key_range_splits():
+    # the same inside one key range of units split over 3 CTAs
+    lay = make_layout("bfloat16", 1, 4, 128, [1000] * 6, 512, 512, 7, seed=91)
+    _scale_block_keys(lay, 4, 40.0)
+    _check(lay, _round_q(_q(91, 1, 16, 320, 128), "bfloat16"), lay.total_tokens - 320)
 
 
 def _prefill_32k_last_chunk(make_q, seed):
