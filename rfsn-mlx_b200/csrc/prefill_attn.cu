@@ -80,7 +80,6 @@ struct Smem {
     uint64_t info_full[NINFO];           // tile info posted (count 1)
     uint64_t s_full[NSB];                // S(t) in TMEM buffer t % NSB
     uint64_t p_full[NSB];                // P(t) written over it (count: softmax threads)
-    uint64_t o_done;                     // PV(t) complete, one phase per tile
     uint64_t pv_done[NSB];               // PV(t) complete, per S/P buffer t % NSB
     uint64_t mma_done;
     uint64_t pair[4][2];  // per 32-row quarter and tile parity: both key halves posted their maxima
@@ -254,7 +253,6 @@ prefill_attn_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
             mbar_init(&sm.p_full[i], SOFTMAX_THREADS);
             mbar_init(&sm.pv_done[i], 1);
         }
-        mbar_init(&sm.o_done, 1);
         mbar_init(&sm.mma_done, 1);
         for (int qd = 0; qd < 4; ++qd) {
             mbar_init(&sm.pair[qd][0], 64);
@@ -373,9 +371,11 @@ prefill_attn_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
                 }
                 const bool issue = sm.tinfo[t % NINFO].y >= 0;
                 if (issue) {
-                    // S buffer t % NSB last held P(t - NSB): PV(t - NSB) must be done. A
-                    // per-buffer barrier: o_done may already be two phases past t - NSB,
-                    // which a parity wait could not tell from the phase itself.
+                    // S buffer t % NSB last held P(t - NSB): PV(t - NSB) must be done.
+                    // Every wait for a PV completion uses the barrier of that PV's
+                    // buffer, whose previous phase (PV(t - 2 NSB)) the issuer has already
+                    // observed: the parity then names the phase, whatever the order in
+                    // which the arrivals of different commits land.
                     if (t >= NSB && !mbar_wait_bounded(&sm.pv_done[t % NSB], ((t / NSB) + 1) & 1, &sm.abort)) {
                         fail(&sm.abort, p);
                         break;
@@ -415,7 +415,6 @@ prefill_attn_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
                                            id_pv, it > 0 || part > 0 || kk > 0);
                         }
                     }
-                    tc::commit(&sm.o_done);
                     tc::commit(&sm.pv_done[it % NSB]);
                     tc::commit(&sm.v_empty[vs]);
                 }
@@ -536,7 +535,7 @@ prefill_attn_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
             l = l * alpha + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
             if (rescale) {
                 // PV of the previous tile must be done before O is rescaled
-                if (!warp_wait(&sm.o_done, (it - 1) & 1, &sm.abort)) { failed = true; break; }
+                if (!warp_wait(&sm.pv_done[(it - 1) % NSB], ((it - 1) / NSB) & 1, &sm.abort)) { failed = true; break; }
                 tc::fence_after_sync();
 #pragma unroll 1
                 for (int cc = 0; cc < 2; ++cc) {
@@ -555,7 +554,7 @@ prefill_attn_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
         // row sum over both key halves. Once the last PV is done the partner has
         // read every maximum posted here (it read them before publishing its P), so
         // red[0] is free for the partial sums.
-        bool ok = !failed && it > 0 && warp_wait(&sm.o_done, (it - 1) & 1, &sm.abort);
+        bool ok = !failed && it > 0 && warp_wait(&sm.pv_done[(it - 1) % NSB], ((it - 1) / NSB) & 1, &sm.abort);
         if (ok) {
             sm.red[0][ch][r] = l;
             mbar_arrive(&sm.pair_l[qd]);
