@@ -157,11 +157,26 @@ constexpr int kPrefillMaxParts = 4;       // split parts per SM at most (bounds 
 struct PrefillPlan {
     int full_units;   // units run whole (the first ones in launch order)
     int tail_splits;  // key ranges of each later unit
+    int head_group;   // KV heads interleaved per band of the launch order
 };
+
+// Launch order: bands of `head_group` KV heads (the last band may be smaller);
+// inside a band, latest query blocks first with the band's heads interleaved.
+// A band's K/V then stays in L2 while its waves stream it. Returns the launch
+// level (0 = latest query block) of unit u.
+inline int prefill_unit_level(int u, int nqb, int groups, int head_group) {
+    const int band = u / (nqb * head_group);
+    const int hs = std::min(head_group, groups - band * head_group);
+    return (u - band * nqb * head_group) / hs;
+}
+
+// K/V bytes of the heads whose units share L2 at once: bands are sized so that
+// about this much of a long context is streamed per band.
+constexpr double kPrefillBandBytes = 48.0 * 1024 * 1024;
 
 // Makespan of greedy list scheduling (each CTA, in launch order, takes the SM
 // that frees first) when the units after the first `full` are split S ways.
-double prefill_makespan(const std::vector<double>& level_tiles, int groups, int full, int S, int sms,
+double prefill_makespan(const std::vector<double>& level_tiles, int groups, int head_group, int full, int S, int sms,
                         std::vector<double>& heap) {
     heap.assign(sms, 0.0);  // all-zero: already a min-heap
     double end = 0.0;
@@ -171,9 +186,9 @@ double prefill_makespan(const std::vector<double>& level_tiles, int groups, int 
         end = std::max(end, heap.back());
         std::push_heap(heap.begin(), heap.end(), std::greater<double>());
     };
-    const int units = (int)level_tiles.size() * groups;
+    const int nqb = (int)level_tiles.size(), units = nqb * groups;
     for (int u = 0; u < units; ++u) {
-        const double t = level_tiles[u / groups];
+        const double t = level_tiles[prefill_unit_level(u, nqb, groups, head_group)];
         if (u < full) {
             place(t + kPrefillCtaCost);
         } else {
@@ -208,19 +223,23 @@ PrefillPlan plan_prefill(int nqb, int groups, int ppc, int q_len, int q_pos0, in
         level[l] = (archived_tokens + hot_keys) / 128.0;
     }
     const int units = nqb * groups;
+    // bands of KV heads whose K/V (16-bit K and V of head_dim 128: 512 bytes per
+    // key) fit the band budget; short contexts interleave every head
+    const double head_bytes = 512.0 * (archived_tokens + hlen);
+    const int head_group = std::max(1, std::min(groups, (int)(kPrefillBandBytes / std::max(head_bytes, 1.0))));
     std::vector<double> heap;
-    PrefillPlan best{units, 1};
-    double best_t = 0.97 * prefill_makespan(level, groups, units, 1, sms, heap);
+    PrefillPlan best{units, 1, head_group};
+    double best_t = 0.97 * prefill_makespan(level, groups, head_group, units, 1, sms, heap);
     const int rem = units % sms;
     for (int S = 2; S <= 4; ++S) {
         for (int tail : {rem, rem + sms, units}) {
             if (tail <= 0 || tail > units || tail > kMaxCounters || (long long)tail * S > (long long)kPrefillMaxParts * sms)
                 continue;
             if (level[nqb - 1] / S < 8.0) continue;  // parts of the shortest units would be mostly overhead
-            const double t = prefill_makespan(level, groups, units - tail, S, sms, heap);
+            const double t = prefill_makespan(level, groups, head_group, units - tail, S, sms, heap);
             if (t < best_t) {
                 best_t = t;
-                best = {units - tail, S};
+                best = {units - tail, S, head_group};
             }
         }
     }
@@ -657,7 +676,7 @@ rfsn_status rfsn::paged_attention_impl(const rfsn_arena* arena, const float* q, 
         const int parts = (units - plan.full_units) * plan.tail_splits;
         WsLayout w = ws_layout(1, 1, plan.tail_splits > 1 ? parts : 1, 128, 128);
         if (w.total > workspace_bytes && plan.tail_splits > 1) {  // a small workspace: run every unit whole
-            plan = {units, 1};
+            plan = {units, 1, plan.head_group};
             w = ws_layout(1, 1, 1, 128, 128);
         }
         if (w.total > workspace_bytes) {
@@ -669,6 +688,7 @@ rfsn_status rfsn::paged_attention_impl(const rfsn_arena* arena, const float* q, 
         pp.nqb = nqb;
         pp.full_units = plan.full_units;
         pp.tail_splits = plan.tail_splits;
+        pp.head_group = plan.head_group;
         pp.q = q;
         pp.out = out;
         pp.lse = lse;

@@ -51,6 +51,7 @@ struct PrefillParams {
     int nqb;                  // query blocks per KV head
     int full_units;           // units (query block, KV head) run whole, in launch order
     int tail_splits;          // key ranges each later unit is split into (1: none)
+    int head_group;           // KV heads whose units are interleaved per band of the launch order
     WsView ws;                // error word; with split units also counters and partial (O, LSE)
 };
 

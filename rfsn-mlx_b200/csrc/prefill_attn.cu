@@ -209,11 +209,13 @@ prefill_attn_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = p.groups_per_kv;
     const int ppc = BM / G;                                   // chunk positions per CTA
-    // Work units (query block, KV head) in launch order: latest query blocks
-    // first (the longest causal key ranges), KV heads interleaved. The first
-    // full_units run whole; each later unit is split into tail_splits key
-    // ranges run by consecutive CTAs, and the last of them to finish merges the
-    // partial results (so the launch's final wave is evenly filled).
+    // Work units (query block, KV head) in launch order: bands of head_group KV
+    // heads (so a band's K/V stays in L2 while its waves stream it), inside a
+    // band latest query blocks first (the longest causal key ranges) with the
+    // band's heads interleaved. The first full_units run whole; each later unit
+    // is split into tail_splits key ranges run by consecutive CTAs, and the last
+    // of them to finish merges the partial results (so the launch's final wave
+    // is evenly filled).
     const int groups = p.batch * p.kv_heads;
     int unit, split, nsplit;
     if ((int)blockIdx.x < p.full_units) {
@@ -227,8 +229,11 @@ prefill_attn_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
         nsplit = p.tail_splits;
     }
     const int tail_index = unit - p.full_units;               // counters and partials of split units
-    const int qb = p.nqb - 1 - unit / groups;
-    const int bh = unit % groups;                             // b * kv_heads + kv head
+    const int band = unit / (p.nqb * p.head_group);
+    const int band_heads = min(p.head_group, groups - band * p.head_group);
+    const int in_band = unit - band * p.nqb * p.head_group;
+    const int qb = p.nqb - 1 - in_band / band_heads;
+    const int bh = band * p.head_group + in_band % band_heads;  // b * kv_heads + kv head
     const int b = bh / p.kv_heads, hk = bh % p.kv_heads;
     const int pos_base = qb * ppc;                            // first chunk position of the CTA
     const int qlast = p.q_pos0 + min(pos_base + ppc, p.q_len) - 1;  // causal limit of the CTA
