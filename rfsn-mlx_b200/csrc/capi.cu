@@ -147,7 +147,8 @@ void preload_kernels_once(int dev) {
 
 // ---- launch plan of the tensor-core prefill ----
 // The kernel runs one CTA per SM; its units (query block, KV head) are
-// launched latest query blocks first. Costs are in 128-key tiles: a CTA costs
+// launched in bands of KV heads, latest query blocks first inside a band
+// (prefill_unit_level below). Costs are in 128-key tiles: a CTA costs
 // its tiles plus a fixed set-up / epilogue share, a split part also the
 // partial write and merge.
 constexpr double kPrefillCtaCost = 4.0;
