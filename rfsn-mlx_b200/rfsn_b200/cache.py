@@ -592,11 +592,6 @@ class LayerKVCache:
             m for m in self.block_manager.page_table.layer_entries(self.layer_id) if m.residency == BlockLocation.WARM_RAM
         ]
 
-    def _cold_manifests(self) -> list[BlockManifest]:
-        return [
-            m for m in self.block_manager.page_table.layer_entries(self.layer_id) if m.residency == BlockLocation.COLD_DISK
-        ]
-
     def _warm_token_count(self) -> int:
         return sum(
             m.token_count

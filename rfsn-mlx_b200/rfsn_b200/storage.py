@@ -294,5 +294,3 @@ class BlockStorage:
         manager.rebuild_from_manifests(manifests)
         return manifests
 
-    def describe(self) -> dict[str, Any]:
-        return {"root_dir": str(self.root_dir), "quarantine_dir": str(self.quarantine_dir)}
