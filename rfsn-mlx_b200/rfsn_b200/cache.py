@@ -238,12 +238,16 @@ class DeviceOps:
             self._upload_stream = torch.cuda.Stream(device=self.device)
         side = self._upload_stream
         side.wait_stream(torch.cuda.current_stream())  # the rows may still be read by earlier kernels
-        done = torch.cuda.Event()
         native.check(
             native.lib().rfsn_block_upload(self.arena.handle, row, n, k.data_ptr(), v.data_ptr(),
-                                           native.stream_ptr(side), done.cuda_event),
+                                           native.stream_ptr(side), None),
             "rfsn_block_upload",
         )
+        # Recorded through torch: a torch.cuda.Event has no CUDA event until torch
+        # records it (its handle reads 0 before), and waiting on an unrecorded one
+        # does nothing.
+        done = torch.cuda.Event()
+        done.record(side)
         torch.cuda.current_stream().wait_event(done)
         self._inflight.append((done, (k, v)))
         self._inflight = [(e, keep) for e, keep in self._inflight if not e.query()]

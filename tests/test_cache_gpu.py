@@ -234,3 +234,23 @@ def test_paged_attention_into_given_output():
             paged_attention(c, q, pos, segs, out=torch.zeros((1, 8, 2, 128), device="cuda"))
         with pytest.raises(ValueError):
             native.host_device_pointer(torch.zeros(4))
+
+
+def test_block_upload_is_ordered_before_the_next_compute_kernel():
+    """DeviceOps.upload copies a block into the arena on a side stream; the
+    compute stream must wait for that copy before its next kernel. A 128 MB
+    block (K and V each) read by the very next kernels on the compute stream
+    shows the uploaded values every time (the copy takes milliseconds over the
+    bus, so a missing wait would show stale rows)."""
+    from rfsn_b200.cache import DeviceOps
+
+    ops = DeviceOps("cuda")
+    groups, n, D = 8, 65536, 128
+    k_arena, v_arena = ops.new_arena(groups, n, D, torch.bfloat16)
+    for trial in range(3):
+        val = float(trial + 1)
+        k = torch.full((groups, n, D), val, dtype=torch.bfloat16).pin_memory()
+        v = torch.full((groups, n, D), -val, dtype=torch.bfloat16).pin_memory()
+        ops.upload(0, n, k, v)
+        assert bool((k_arena == val).all()) and bool((v_arena == -val).all()), trial
+    torch.cuda.synchronize()
