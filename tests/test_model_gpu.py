@@ -256,6 +256,8 @@ def test_decode_graph_falls_back_when_blocks_are_cold(tmp_path):
 
     eager, c_e = make(False, "e")
     graphed, c_g = make(True, "g")
+    for c in (c_e, c_g):  # prefetch loads on the caller's thread: one residency schedule for both models
+        c.layer(0).residency_manager.inline_loads = True
     prompt = torch.randint(0, 256, (1, 200), generator=torch.Generator().manual_seed(14))
     le = eager.prefill(prompt, c_e)
     graphed.prefill(prompt, c_g)
