@@ -93,20 +93,16 @@ struct Smem {
 };
 
 // (a, b) -> packed 16-bit high parts and packed 16-bit residuals (a = hi + lo to
-// ~16 significand bits). bf16: rounding by integer add on the bit pattern (half
-// away from zero on the magnitude; the inputs are finite) and a byte permute,
-// which keeps the conversions off the special-function pipe that runs exp2.
+// ~16 significand bits): both packs by the round-to-nearest pair conversion
+// (cvt.rn.{bf16x2,f16x2}.f32, one instruction per pair). For bf16 the high parts
+// widen back to float32 by a shift or a mask of the packed word, so the exact
+// residuals cost two subtractions.
 template <typename T>
 __device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
+    hi = pack2<T>(a, b);
     if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-        const uint32_t ha = (__float_as_uint(a) + 0x8000u) & 0xffff0000u;
-        const uint32_t hb = (__float_as_uint(b) + 0x8000u) & 0xffff0000u;
-        const uint32_t la = __float_as_uint(a - __uint_as_float(ha)) + 0x8000u;
-        const uint32_t lb = __float_as_uint(b - __uint_as_float(hb)) + 0x8000u;
-        hi = __byte_perm(ha, hb, 0x7632);
-        lo = __byte_perm(la, lb, 0x7632);
+        lo = pack2<T>(a - __uint_as_float(hi << 16), b - __uint_as_float(hi & 0xffff0000u));
     } else {
-        hi = pack2<T>(a, b);
         const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hi));
         lo = pack2<T>(a - f.x, b - f.y);
     }
