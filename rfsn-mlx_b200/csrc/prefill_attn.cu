@@ -92,6 +92,37 @@ struct Smem {
     int q_lo;  // some q element of the CTA has a nonzero 16-bit residual
 };
 
+// Paired float32 arithmetic (PTX .f32x2, sm_100): two lanes of work per
+// instruction issue, each rounded as the scalar operation.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+        "mov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "add.rn.f32x2 rd, ra, rb;\n\t"
+        "mov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+__device__ __forceinline__ float2 fsub2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "sub.rn.f32x2 rd, ra, rb;\n\t"
+        "mov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+
 // (a, b) -> packed 16-bit high parts and packed 16-bit residuals (a = hi + lo to
 // ~16 significand bits): both packs by the round-to-nearest pair conversion
 // (cvt.rn.{bf16x2,f16x2}.f32, one instruction per pair). For bf16 the high parts
@@ -101,7 +132,8 @@ template <typename T>
 __device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
     hi = pack2<T>(a, b);
     if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-        lo = pack2<T>(a - __uint_as_float(hi << 16), b - __uint_as_float(hi & 0xffff0000u));
+        const float2 r = fsub2(make_float2(a, b), make_float2(__uint_as_float(hi << 16), __uint_as_float(hi & 0xffff0000u)));
+        lo = pack2<T>(r.x, r.y);
     } else {
         const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hi));
         lo = pack2<T>(a - f.x, b - f.y);
@@ -521,15 +553,17 @@ prefill_attn_kernel(const __grid_constant__ CUtensorMap mapK64, const __grid_con
                 m = mn;
             }
             const float ms = (m == -CUDART_INF_F) ? 0.f : m;
-            float rs[4] = {0.f, 0.f, 0.f, 0.f};
+            const float2 qs2 = make_float2(p.qscale, p.qscale), nms2 = make_float2(-ms, -ms);
+            float2 rs2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
             uint32_t hi[32], lo[32];
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
-                const float p0 = tc::ex2(fmaf(__uint_as_float(sr[2 * e]), p.qscale, -ms));
-                const float p1 = tc::ex2(fmaf(__uint_as_float(sr[2 * e + 1]), p.qscale, -ms));
-                rs[e & 3] += p0 + p1;
-                split2<T>(p0, p1, hi[e], lo[e]);
+                const float2 x = ffma2(make_float2(__uint_as_float(sr[2 * e]), __uint_as_float(sr[2 * e + 1])), qs2, nms2);
+                const float2 pp = make_float2(tc::ex2(x.x), tc::ex2(x.y));
+                rs2[e & 1] = fadd2(rs2[e & 1], pp);
+                split2<T>(pp.x, pp.y, hi[e], lo[e]);
             }
+            const float rs[4] = {rs2[0].x, rs2[0].y, rs2[1].x, rs2[1].y};
             // P columns: key k of the tile -> 16-bit element k (column k / 2); lo after hi
             tc::st_32x32b_x32(tS + 32 * ch, hi);
             tc::st_32x32b_x32(tS + 64 + 32 * ch, lo);
