@@ -219,7 +219,7 @@ RFSN_API rfsn_status rfsn_gemv(const void* weight, const void* x, void* y, int n
 /* Launch plan of a tensor-core prefill call of this shape (rfsn_paged_attention
  * with q_len >= 64, bf16/f16 K/V, head_dim 128): the units (query block of
  * 128 / (q_heads / kv_heads) positions x KV head) are launched in bands of KV
- * heads whose K/V fits 48 MB of L2 (all heads in one band for short contexts),
+ * heads whose K/V fits 40 MB of L2 (all heads in one band for short contexts),
  * longest causal range first inside a band; the first *cta_units_whole run
  * whole, each later one is split
  * into *tail_splits key ranges whose last CTA merges them; *ctas CTAs in all.

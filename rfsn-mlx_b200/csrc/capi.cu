@@ -173,7 +173,7 @@ inline int prefill_unit_level(int u, int nqb, int groups, int head_group) {
 
 // K/V bytes of the heads whose units share L2 at once: bands are sized so that
 // about this much of a long context is streamed per band.
-constexpr double kPrefillBandBytes = 48.0 * 1024 * 1024;
+constexpr double kPrefillBandBytes = 40.0 * 1024 * 1024;
 
 // Makespan of greedy list scheduling (each CTA, in launch order, takes the SM
 // that frees first) when the units after the first `full` are split S ways.
